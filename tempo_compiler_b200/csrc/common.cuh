@@ -1,0 +1,267 @@
+// Shared device helpers for the sm_100a kernels: BF16 conversion, mbarriers with bounded waits, TMA tensor loads,
+// and the tcgen05 (5th-generation tensor core) instructions with their shared-memory and instruction descriptors.
+//
+// Every wait on an mbarrier is bounded: after kWaitLimitNs of global time the waiting thread records a watchdog
+// error (g_tempo_watchdog) and returns false, so a pipeline bug ends the kernel with a status the host reads
+// instead of hanging the GPU.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tempo {
+
+// ---------------------------------------------------------------------------------------------------------------
+// Watchdog
+// ---------------------------------------------------------------------------------------------------------------
+
+// Set (to a code naming the wait that gave up) by any bounded wait that expires. One copy per translation unit;
+// each unit that waits defines a host reader with TEMPO_WATCHDOG_READER, which the runtime polls and clears.
+static __device__ int g_tempo_watchdog = 0;
+
+#define TEMPO_WATCHDOG_READER(fn)                                            \
+  int fn() {                                                                 \
+    int value = 0, zero = 0;                                                 \
+    if (cudaMemcpyFromSymbol(&value, g_tempo_watchdog, sizeof(int)) != cudaSuccess) return -1; \
+    if (value != 0) cudaMemcpyToSymbol(g_tempo_watchdog, &zero, sizeof(int)); \
+    return value;                                                            \
+  }
+
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s of global time per wait
+
+enum WatchdogCode : int {
+  kWatchFull = 1,      // consumer waiting for a TMA stage
+  kWatchEmpty = 2,     // producer waiting for a free stage
+  kWatchAccFull = 3,   // epilogue waiting for the accumulator
+  kWatchAccEmpty = 4,  // MMA waiting for the epilogue to drain the accumulator
+  kWatchOther = 5,
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// BF16
+// ---------------------------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ float bf16_lo(uint32_t pair) { return __uint_as_float(pair << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t pair) { return __uint_as_float(pair & 0xFFFF0000u); }
+__device__ __forceinline__ float bf16_to_float(uint16_t word) { return __uint_as_float(uint32_t(word) << 16); }
+
+// Round-to-nearest-even float -> BF16 (cuda_bf16's conversion is RNE).
+__device__ __forceinline__ uint16_t float_to_bf16(float v) {
+  __nv_bfloat16 b = __float2bfloat16_rn(v);
+  return *reinterpret_cast<uint16_t*>(&b);
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+__device__ __forceinline__ float round_bf16(float v) { return bf16_to_float(float_to_bf16(v)); }
+
+// Exact-erf GELU of a float, 0.5 x (1 + erf(x / sqrt 2)).
+__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f)); }
+
+// ---------------------------------------------------------------------------------------------------------------
+// Shared memory addressing and mbarriers
+// ---------------------------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits for the phase with the given parity to complete. Returns false (and records `code`) if it has not after
+// kWaitLimitNs, or if `abort` (a shared flag another role sets when it gives up) becomes non-zero.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code, volatile int* abort) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const unsigned long long start = global_ns();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try_wait(addr, parity)) return true;
+    if ((spin & 255u) == 0u) {
+      if (abort != nullptr && *abort) return false;
+      if (global_ns() - start > kWaitLimitNs) {
+        atomicExch(&g_tempo_watchdog, code);
+        if (abort != nullptr) *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// TMA (tensor memory accelerator) loads into shared memory, completing on an mbarrier
+// ---------------------------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t c0, int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t c0, int32_t c1,
+                                            int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t c0, int32_t c1,
+                                            int32_t c2, int32_t c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
+        "r"(c3)
+      : "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads (tcgen05.mma operands).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// tcgen05: tensor memory allocation, MMA, commit, loads
+// ---------------------------------------------------------------------------------------------------------------
+
+// Allocates `columns` (a power of two >= 32) TMEM columns; the base address lands in *dst (shared memory). Must be
+// executed by one whole warp.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t columns) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(columns)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t columns) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(columns) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem desc] x B[smem desc], kind::f16 (BF16 inputs, FP32 accumulate per the instruction descriptor).
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on `bar` when every tcgen05 operation this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 bits, 32 consecutive columns: thread t of the warp receives lane (base lane + t), columns c..c+31.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// UMMA descriptors
+// ---------------------------------------------------------------------------------------------------------------
+
+// Shared-memory matrix descriptor layout types (sm_100).
+enum : uint32_t { kLayoutNone = 0, kLayoutSw128 = 2, kLayoutSw64 = 4, kLayoutSw32 = 6 };
+
+// Builds a shared-memory matrix descriptor: start address, leading/stride byte offsets (bytes, multiples of 16),
+// version 1 (Blackwell), base offset 0 (the swizzle atom is aligned), and the layout type.
+__device__ __forceinline__ uint64_t make_smem_desc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                                   uint32_t layout) {
+  uint64_t desc = 0;
+  desc |= uint64_t((smem_addr >> 4) & 0x3FFFu);
+  desc |= uint64_t((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  desc |= uint64_t((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  desc |= uint64_t(1) << 46;
+  desc |= uint64_t(layout & 0x7u) << 61;
+  return desc;
+}
+
+// Instruction descriptor for kind::f16 with BF16 A and B, FP32 D. a_mn/b_mn select MN-major operands.
+__host__ __device__ constexpr uint32_t make_idesc_bf16(uint32_t m, uint32_t n, uint32_t a_mn, uint32_t b_mn) {
+  return (1u << 4)          // D format: F32
+         | (1u << 7)        // A format: BF16
+         | (1u << 10)       // B format: BF16
+         | (a_mn << 15)     // A major
+         | (b_mn << 16)     // B major
+         | ((n >> 3) << 17)  // N / 8
+         | ((m >> 4) << 24);  // M / 16
+}
+
+__device__ __forceinline__ uint32_t warp_id() { return threadIdx.x >> 5; }
+__device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xFFFFFFFF;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+}  // namespace tempo

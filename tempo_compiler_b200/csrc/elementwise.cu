@@ -1,0 +1,309 @@
+// Bandwidth-bound kernels: the residual add and bias add, LayerNorm, the KV-cache copies, the embedding gather,
+// the KV store of the native engine and the argmax reduction. 128-bit vector loads and stores throughout; row
+// reductions are warp shuffles.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "host.hpp"
+
+namespace tempo {
+namespace {
+
+constexpr uint32_t kBlockTokens = 32;
+constexpr uint32_t kTile = 16;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& w, float (&f)[8]) {
+  f[0] = bf16_lo(w.x); f[1] = bf16_hi(w.x); f[2] = bf16_lo(w.y); f[3] = bf16_hi(w.y);
+  f[4] = bf16_lo(w.z); f[5] = bf16_hi(w.z); f[6] = bf16_lo(w.w); f[7] = bf16_hi(w.w);
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 w;
+  w.x = pack_bf16x2(f[0], f[1]); w.y = pack_bf16x2(f[2], f[3]);
+  w.z = pack_bf16x2(f[4], f[5]); w.w = pack_bf16x2(f[6], f[7]);
+  return w;
+}
+
+// ---- packed block add: out = round(left + right) or round(left + bias row t%4), 8 values per thread ----
+__global__ void block_add_kernel(const uint4* __restrict__ left, const uint4* __restrict__ right,
+                                 uint4* __restrict__ out, uint32_t vectors, uint32_t broadcast) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= vectors) return;
+  float a[8], b[8];
+  unpack8(left[i], a);
+  if (broadcast) {
+    // Vector i covers values 8i..8i+7 of [tiles][32][16]: tile i/64, token (i/2)%32, half i%2.
+    const uint32_t tile = i >> 6, token = (i >> 1) & 31u, half = i & 1u;
+    unpack8(right[(tile * 4 + (token & 3u)) * 2 + half], b);
+  } else {
+    unpack8(right[i], b);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) a[j] += b[j];
+  out[i] = pack8(a);
+}
+
+// ---- packed block LayerNorm: one warp per token; features strided 1 KB apart in 16-wide tiles ----
+__global__ void block_layernorm_kernel(const uint16_t* __restrict__ rows, const uint16_t* __restrict__ constants,
+                                       uint16_t* __restrict__ out, uint32_t features) {
+  const uint32_t token = blockIdx.x * (blockDim.x / 32) + warp_id();
+  if (token >= kBlockTokens) return;
+  const uint32_t lane = lane_id();
+  const uint32_t chunks = features / 8;  // 16-byte chunks per token
+  auto chunk_offset = [&](uint32_t c) { return (c >> 1) * (kBlockTokens * kTile) + token * kTile + (c & 1u) * 8; };
+  const float inverse = bf16_to_float(constants[2 * features]);
+  const float epsilon = bf16_to_float(constants[2 * features + 64]);
+  float sum = 0.f;
+  for (uint32_t c = lane; c < chunks; c += 32) {
+    float f[8];
+    unpack8(*reinterpret_cast<const uint4*>(rows + chunk_offset(c)), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sum += f[j];
+  }
+  const float mean = warp_sum(sum) * inverse;
+  float sq = 0.f;
+  for (uint32_t c = lane; c < chunks; c += 32) {
+    float f[8];
+    unpack8(*reinterpret_cast<const uint4*>(rows + chunk_offset(c)), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sq += (f[j] - mean) * (f[j] - mean);
+  }
+  const float scale = rsqrtf(warp_sum(sq) * inverse + epsilon);
+  for (uint32_t c = lane; c < chunks; c += 32) {
+    float f[8], g[8], b[8];
+    unpack8(*reinterpret_cast<const uint4*>(rows + chunk_offset(c)), f);
+    unpack8(*reinterpret_cast<const uint4*>(constants + c * 8), g);
+    unpack8(*reinterpret_cast<const uint4*>(constants + features + c * 8), b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = (f[j] - mean) * scale * g[j] + b[j];
+    *reinterpret_cast<uint4*>(out + chunk_offset(c)) = pack8(f);
+  }
+}
+
+// ---- packed row copy: `rows` 32-byte rows, `stride` bytes apart at both ends; 4-byte words ----
+__global__ void block_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, uint32_t rows,
+                                  uint32_t stride) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;  // word index: 8 words per row
+  if (i >= rows * 8) return;
+  const size_t offset = size_t(i >> 3) * stride + (i & 7u) * 4;
+  *reinterpret_cast<uint32_t*>(dst + offset) = *reinterpret_cast<const uint32_t*>(src + offset);
+}
+
+// ---- native LayerNorm: one warp per row, CPL 16-byte chunks per lane held in registers ----
+template <int CPL>
+__global__ void layernorm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma,
+                                 const uint16_t* __restrict__ beta, uint16_t* __restrict__ out, uint32_t rows,
+                                 uint32_t features, float epsilon) {
+  const uint32_t row = blockIdx.x * (blockDim.x / 32) + warp_id();
+  if (row >= rows) return;
+  const uint32_t lane = lane_id();
+  const uint32_t chunks = features / 8;
+  const uint16_t* xr = x + size_t(row) * features;
+  float v[CPL][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const uint32_t c = lane + 32u * i;
+    if (c < chunks) {
+      unpack8(*reinterpret_cast<const uint4*>(xr + c * 8), v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += v[i][j];
+    }
+  }
+  const float inv_f = 1.0f / float(features);
+  const float mean = warp_sum(sum) * inv_f;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    if (lane + 32u * i < chunks) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sq += (v[i][j] - mean) * (v[i][j] - mean);
+    }
+  }
+  const float scale = rsqrtf(warp_sum(sq) * inv_f + epsilon);
+  uint16_t* orow = out + size_t(row) * features;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const uint32_t c = lane + 32u * i;
+    if (c < chunks) {
+      float g[8], b[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(gamma + c * 8)), g);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(beta + c * 8)), b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = (v[i][j] - mean) * scale * g[j] + b[j];
+      *reinterpret_cast<uint4*>(orow + c * 8) = pack8(v[i]);
+    }
+  }
+}
+
+// ---- embedding gather: x[r] = round(wte[ids[r]] + wpe[pos[r]]) ----
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ positions,
+                             const uint16_t* __restrict__ wte, const uint16_t* __restrict__ wpe,
+                             uint16_t* __restrict__ x, uint32_t rows, uint32_t width, uint32_t vocab,
+                             uint32_t max_positions) {
+  const uint32_t per_row = width / 8;
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * per_row) return;
+  const uint32_t r = i / per_row, c = i % per_row;
+  if (uint32_t(ids[r]) >= vocab || uint32_t(positions[r]) >= max_positions) {
+    reinterpret_cast<uint4*>(x + size_t(r) * width)[c] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  float a[8], b[8];
+  unpack8(__ldg(reinterpret_cast<const uint4*>(wte + size_t(ids[r]) * width) + c), a);
+  unpack8(__ldg(reinterpret_cast<const uint4*>(wpe + size_t(positions[r]) * width) + c), b);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) a[j] += b[j];
+  reinterpret_cast<uint4*>(x + size_t(r) * width)[c] = pack8(a);
+}
+
+// ---- KV store: keys and values of qkv rows into [seq][head][capacity][head_dim] caches ----
+__global__ void kv_store_kernel(const uint16_t* __restrict__ qkv, uint16_t* __restrict__ k_cache,
+                                uint16_t* __restrict__ v_cache, const int32_t* __restrict__ seq_of,
+                                const int32_t* __restrict__ pos_of, uint32_t rows, uint32_t seqs, uint32_t heads,
+                                uint32_t head, uint32_t capacity) {
+  const uint32_t width = heads * head;
+  const uint32_t per_row = 2 * width / 8;  // 16-byte vectors of keys then values
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * per_row) return;
+  const uint32_t r = i / per_row, c = i % per_row;
+  if (uint32_t(seq_of[r]) >= seqs || uint32_t(pos_of[r]) >= capacity) return;
+  const uint32_t which = (c * 8) / width;       // 0 keys, 1 values
+  const uint32_t feature = (c * 8) % width;
+  const uint32_t h = feature / head, d = feature % head;
+  const uint4 w = reinterpret_cast<const uint4*>(qkv + size_t(r) * 3 * width + width + which * width + feature)[0];
+  uint16_t* cache = which ? v_cache : k_cache;
+  const size_t slot = ((size_t(seq_of[r]) * heads + h) * capacity + size_t(pos_of[r])) * head + d;
+  *reinterpret_cast<uint4*>(cache + slot) = w;
+}
+
+// ---- argmax reduction over the LM head's per-tile partials; first index wins ties ----
+__global__ void argmax_finish_kernel(const float* __restrict__ part_val, const int32_t* __restrict__ part_idx,
+                                     uint32_t rows, uint32_t tiles, int32_t* __restrict__ ids,
+                                     int32_t* __restrict__ tokens_out, uint32_t out_stride,
+                                     int32_t* __restrict__ positions, int32_t advance) {
+  const uint32_t row = blockIdx.x * (blockDim.x / 32) + warp_id();
+  if (row >= rows) return;
+  const uint32_t lane = lane_id();
+  float best = -INFINITY;
+  int32_t idx = 0x7FFFFFFF;
+  for (uint32_t t = lane; t < tiles; t += 32) {
+    const float v = part_val[size_t(row) * tiles + t];
+    const int32_t i = part_idx[size_t(row) * tiles + t];
+    if (v > best || (v == best && i < idx)) { best = v; idx = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+    const int32_t oi = __shfl_xor_sync(0xFFFFFFFFu, idx, o);
+    if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
+  }
+  if (lane == 0) {
+    ids[row] = idx;
+    if (tokens_out != nullptr) tokens_out[size_t(row) * out_stride] = idx;
+    if (positions != nullptr) positions[row] += advance;
+  }
+}
+
+}  // namespace
+}  // namespace tempo
+
+using namespace tempo;
+
+extern "C" tempo_status tempo_block_add(const void* left, const void* right, void* out, uint32_t features,
+                                        uint32_t broadcast, void* stream) {
+  if (features == 0 || features % 16) return fail(TEMPO_ERR_VALUE, "tempo_block_add: features %u", features);
+  if (!aligned16(left) || !aligned16(right) || !aligned16(out))
+    return fail(TEMPO_ERR_VALUE, "tempo_block_add: operands must be 16-byte aligned");
+  const uint32_t vectors = kBlockTokens * features / 8;
+  block_add_kernel<<<(vectors + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(left), static_cast<const uint4*>(right), static_cast<uint4*>(out), vectors,
+      broadcast);
+  return check_launch("block_add_kernel");
+}
+
+extern "C" tempo_status tempo_block_layernorm(const void* rows, const void* constants, void* out, uint32_t features,
+                                              void* stream) {
+  if (features == 0 || features % 16) return fail(TEMPO_ERR_VALUE, "tempo_block_layernorm: features %u", features);
+  if (!aligned16(rows) || !aligned16(constants) || !aligned16(out))
+    return fail(TEMPO_ERR_VALUE, "tempo_block_layernorm: operands must be 16-byte aligned");
+  block_layernorm_kernel<<<4, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(rows), static_cast<const uint16_t*>(constants), static_cast<uint16_t*>(out),
+      features);
+  return check_launch("block_layernorm_kernel");
+}
+
+extern "C" tempo_status tempo_block_copy(const void* source, void* destination, uint32_t rows, uint32_t stride,
+                                         void* stream) {
+  if (rows == 0 || stride < 32) return fail(TEMPO_ERR_VALUE, "tempo_block_copy: rows %u stride %u", rows, stride);
+  if ((reinterpret_cast<uintptr_t>(source) | reinterpret_cast<uintptr_t>(destination) | stride) & 3u)
+    return fail(TEMPO_ERR_VALUE, "tempo_block_copy: addresses and stride must be 4-byte aligned");
+  const uint32_t words = rows * 8;
+  block_copy_kernel<<<(words + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(source), static_cast<uint8_t*>(destination), rows, stride);
+  return check_launch("block_copy_kernel");
+}
+
+extern "C" tempo_status tempo_layernorm(const void* x, const void* gamma, const void* beta, void* out, uint32_t rows,
+                                        uint32_t features, float epsilon, void* stream) {
+  if (rows == 0 || features == 0 || features % 8 || features > 4096)
+    return fail(TEMPO_ERR_VALUE, "tempo_layernorm: rows %u features %u", rows, features);
+  if (!aligned16(x) || !aligned16(gamma) || !aligned16(beta) || !aligned16(out))
+    return fail(TEMPO_ERR_VALUE, "tempo_layernorm: operands must be 16-byte aligned");
+  const uint32_t cpl = (features / 8 + 31) / 32;
+  const dim3 grid((rows + 7) / 8), block(256);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* xs = static_cast<const uint16_t*>(x);
+  auto* gs = static_cast<const uint16_t*>(gamma);
+  auto* bs = static_cast<const uint16_t*>(beta);
+  auto* os = static_cast<uint16_t*>(out);
+  if (cpl <= 1) layernorm_kernel<1><<<grid, block, 0, st>>>(xs, gs, bs, os, rows, features, epsilon);
+  else if (cpl <= 2) layernorm_kernel<2><<<grid, block, 0, st>>>(xs, gs, bs, os, rows, features, epsilon);
+  else if (cpl <= 3) layernorm_kernel<3><<<grid, block, 0, st>>>(xs, gs, bs, os, rows, features, epsilon);
+  else if (cpl <= 4) layernorm_kernel<4><<<grid, block, 0, st>>>(xs, gs, bs, os, rows, features, epsilon);
+  else if (cpl <= 8) layernorm_kernel<8><<<grid, block, 0, st>>>(xs, gs, bs, os, rows, features, epsilon);
+  else layernorm_kernel<16><<<grid, block, 0, st>>>(xs, gs, bs, os, rows, features, epsilon);
+  return check_launch("layernorm_kernel");
+}
+
+extern "C" tempo_status tempo_embed(const int32_t* ids, const int32_t* positions, const void* wte, const void* wpe,
+                                    void* x, uint32_t rows, uint32_t width, uint32_t vocab, uint32_t max_positions,
+                                    void* stream) {
+  if (rows == 0 || width == 0 || width % 8) return fail(TEMPO_ERR_VALUE, "tempo_embed: rows %u width %u", rows, width);
+  if (!aligned16(wte) || !aligned16(wpe) || !aligned16(x))
+    return fail(TEMPO_ERR_VALUE, "tempo_embed: operands must be 16-byte aligned");
+  const uint64_t threads = uint64_t(rows) * (width / 8);
+  embed_kernel<<<uint32_t((threads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      ids, positions, static_cast<const uint16_t*>(wte), static_cast<const uint16_t*>(wpe), static_cast<uint16_t*>(x),
+      rows, width, vocab, max_positions);
+  return check_launch("embed_kernel");
+}
+
+extern "C" tempo_status tempo_kv_store(const void* qkv, void* k_cache, void* v_cache, const int32_t* seq_of,
+                                       const int32_t* pos_of, uint32_t rows, uint32_t seqs, uint32_t heads,
+                                       uint32_t head, uint32_t capacity, void* stream) {
+  if (rows == 0 || heads == 0 || head == 0 || head % 8 || capacity == 0)
+    return fail(TEMPO_ERR_VALUE, "tempo_kv_store: rows %u heads %u head %u capacity %u", rows, heads, head, capacity);
+  if (!aligned16(qkv) || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(TEMPO_ERR_VALUE, "tempo_kv_store: operands must be 16-byte aligned");
+  const uint64_t threads = uint64_t(rows) * (2 * heads * head / 8);
+  kv_store_kernel<<<uint32_t((threads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(qkv), static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), seq_of,
+      pos_of, rows, seqs, heads, head, capacity);
+  return check_launch("kv_store_kernel");
+}
+
+extern "C" tempo_status tempo_argmax_finish(const float* part_val, const int32_t* part_idx, uint32_t rows,
+                                            uint32_t tiles, int32_t* ids, int32_t* tokens_out, uint32_t out_stride,
+                                            int32_t* positions, int32_t advance, void* stream) {
+  if (rows == 0 || tiles == 0) return fail(TEMPO_ERR_VALUE, "tempo_argmax_finish: rows %u tiles %u", rows, tiles);
+  argmax_finish_kernel<<<(rows + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      part_val, part_idx, rows, tiles, ids, tokens_out, out_stride, positions, advance);
+  return check_launch("argmax_finish_kernel");
+}

@@ -1,0 +1,536 @@
+// BF16 GEMMs on the 5th-generation tensor cores: TMA-fed, tcgen05.mma into TMEM accumulators, FP32 accumulate.
+//
+// Two kernels share the same warp-specialised pipeline (warp 0: TMA producer, warp 1: MMA issuer and TMEM owner,
+// warps 2-5: epilogue):
+//
+//  * gemm_rowmajor_kernel -- the native engine's GEMM, out[M,N] = A[M,K] x W^T[N,K]^T, 128 x BN tiles, 64-deep
+//    stages in the 128-byte swizzled K-major layout, a persistent tile loop and a double-buffered accumulator so the
+//    epilogue of one tile overlaps the MMAs of the next. Epilogue: + bias, exact-erf GELU, + residual, BF16 store;
+//    or a fused argmax over the tile for the LM head.
+//
+//  * gemm_block_kernel -- one 32-token block on the packed drop-in layouts (gemm_resident,
+//    board_package/gpt2_inference.py:574-640; tile op mlir/include/tempo/tempo/tempo_ops.td:228-252). The weights'
+//    16-column tiles ([columns/16][depth][16]) are the MMA's M side in the MN-major 32-byte swizzled layout and the
+//    block's 16-deep activation tiles ([depth/16][32][16]) its N side in the K-major 32-byte swizzled layout, so both
+//    operands stream straight from the packed tensors by TMA with no repacking (UMMA 128 x 32 x 16). With
+//    `activate`, the epilogue warps pass each staged activation tile through the exact-erf GELU in shared memory
+//    before the MMA reads it (the reference applies its GELU while staging, tile_to_vector.cpp:239-256).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "host.hpp"
+
+namespace tempo {
+
+TEMPO_WATCHDOG_READER(watchdog_gemm)
+
+namespace {
+
+constexpr int kThreads = 192;  // 6 warps
+constexpr int kBK = 64;        // 64 BF16 = 128 bytes: one 128B-swizzle atom row
+
+struct RowMajorParams {
+  const uint16_t* bias;
+  const uint16_t* residual;
+  uint16_t* out;
+  float* part_val;
+  int32_t* part_idx;
+  uint32_t m, n, k;
+  uint32_t ldo, ldr;
+  uint32_t flags;
+  uint32_t m_tiles, n_tiles;
+};
+
+template <int BN, int STAGES>
+struct RowMajorSmem {
+  static constexpr uint32_t kABytes = 128 * kBK * 2;
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kBarrierOffset = STAGES * kStageBytes;
+  // full[S], empty[S], acc_full[2], acc_empty[2], final
+  static constexpr uint32_t kBarriers = 2 * STAGES + 5;
+  static constexpr uint32_t kBytes = kBarrierOffset + kBarriers * 8 + 16 + 1024;  // + tmem slot, abort, alignment
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_rowmajor_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                         RowMajorParams p) {
+  using L = RowMajorSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarrierOffset);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;
+  uint64_t* final_bar = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kBarriers);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const uint32_t tiles = p.m_tiles * p.n_tiles;
+  const uint32_t kblocks = (p.k + kBK - 1) / kBK;
+  constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      uint32_t stage = 0, phase = 0;
+      uint32_t last_parity[STAGES];
+      bool used[STAGES];
+      for (int s = 0; s < STAGES; ++s) used[s] = false;
+      bool ok = true;
+      for (uint32_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int32_t m0 = int32_t((t / p.n_tiles) * 128);
+        const int32_t n0 = int32_t((t % p.n_tiles) * BN);
+        for (uint32_t kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, kWatchEmpty, abort_flag)) { ok = false; break; }
+          uint8_t* a_dst = smem + stage * L::kStageBytes;
+          uint8_t* b_dst = a_dst + L::kABytes;
+          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          tma_load_2d(a_dst, &tmap_a, &full[stage], int32_t(kb * kBK), m0);
+          tma_load_2d(b_dst, &tmap_b, &full[stage], int32_t(kb * kBK), n0);
+          used[stage] = true;
+          last_parity[stage] = phase;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Every copy this thread issued must have landed before the CTA may exit.
+      for (int s = 0; s < STAGES; ++s)
+        if (used[s]) mbar_wait(&full[s], last_parity[s], kWatchFull, nullptr);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc_bf16(128, BN, 0, 0);
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (uint32_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, kWatchAccEmpty, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (uint32_t kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, kWatchFull, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+          for (uint32_t kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t a_desc = make_smem_desc(a_addr + kk * 32, 16, 1024, kLayoutSw128);
+            const uint64_t b_desc = make_smem_desc(b_addr + kk * 32, 16, 1024, kLayoutSw128);
+            umma_bf16(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+        acc ^= 1u;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // Drain every MMA this thread issued before the accumulator is freed.
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, kWatchOther, nullptr);
+    }
+  } else {
+    // Epilogue: warps 2..5 own TMEM lanes 32*(warp%4) .. +31, i.e. tile rows.
+    const uint32_t lane_base = 32u * (warp & 3u);
+    const uint32_t row_in_tile = lane_base + lane;
+    uint32_t acc = 0, acc_phase = 0;
+    const bool gelu = (p.flags & TEMPO_GEMM_GELU) != 0;
+    const bool argmax = (p.flags & TEMPO_GEMM_ARGMAX) != 0;
+    for (uint32_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+      if (!mbar_wait(&acc_full[acc], acc_phase, kWatchAccFull, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t m_blk = t / p.n_tiles, n_blk = t % p.n_tiles;
+      const uint32_t row = m_blk * 128 + row_in_tile;
+      const bool row_ok = row < p.m;
+      float best = -INFINITY;
+      int32_t best_idx = 0;
+#pragma unroll 1
+      for (uint32_t c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + acc * BN + c, r);
+        tmem_wait_ld();
+        const uint32_t n0 = n_blk * BN + c;
+        if (!row_ok || n0 >= p.n) continue;
+        if (argmax) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float v = __uint_as_float(r[j]);
+            if (n0 + j < p.n && v > best) { best = v; best_idx = int32_t(n0 + j); }
+          }
+          continue;
+        }
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        const bool full_chunk = n0 + 32 <= p.n;
+        if (p.bias != nullptr) {
+          if (full_chunk) {
+            const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 w = __ldg(b4 + q);
+              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                v[q * 8 + 2 * h] += bf16_lo(ws[h]);
+                v[q * 8 + 2 * h + 1] += bf16_hi(ws[h]);
+              }
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.n) v[j] += bf16_to_float(p.bias[n0 + j]);
+          }
+        }
+        if (gelu) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = gelu_erf(round_bf16(v[j]));
+        }
+        uint16_t* orow = p.out + size_t(row) * p.ldo;
+        if (p.residual != nullptr) {
+          const uint16_t* rrow = p.residual + size_t(row) * p.ldr;
+          if (full_chunk) {
+            const uint4* r4 = reinterpret_cast<const uint4*>(rrow + n0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 w = r4[q];
+              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                v[q * 8 + 2 * h] += bf16_lo(ws[h]);
+                v[q * 8 + 2 * h + 1] += bf16_hi(ws[h]);
+              }
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < p.n) v[j] += bf16_to_float(rrow[n0 + j]);
+          }
+        }
+        if (full_chunk) {
+          uint4* o4 = reinterpret_cast<uint4*>(orow + n0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+            w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+            w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+            w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+            o4[q] = w;
+          }
+        } else {
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.n) orow[n0 + j] = float_to_bf16(v[j]);
+        }
+      }
+      if (argmax && row_ok) {
+        p.part_val[size_t(row) * p.n_tiles + n_blk] = best;
+        p.part_idx[size_t(row) * p.n_tiles + n_blk] = best_idx;
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      acc ^= 1u;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Packed per-block GEMM (swap-AB: UMMA M = 128 output columns, N = 32 tokens)
+// ---------------------------------------------------------------------------------------------------------------
+
+struct BlockParams {
+  const uint16_t* bias;  // [columns/16][4][16] or null
+  uint16_t* drain;       // zero tile, then [columns/16][32][16]
+  uint32_t depth, columns;
+  uint32_t activate;
+};
+
+constexpr int kBlockStages = 4;
+constexpr uint32_t kBlockW = 128 * kBK * 2;  // 8 column tiles x 64 deep x 16
+constexpr uint32_t kBlockA = 32 * kBK * 2;   // 4 k tiles x 32 tokens x 16
+constexpr uint32_t kBlockStage = kBlockW + kBlockA;
+constexpr uint32_t kBlockOut = 128 * 32 * 2;  // the CTA's 8 output tiles
+constexpr uint32_t kBlockBarrierOffset = kBlockStages * kBlockStage + kBlockOut;
+constexpr uint32_t kBlockBarriers = 3 * kBlockStages + 2;  // full, ready, empty, acc_full, final
+constexpr uint32_t kBlockSmem = kBlockBarrierOffset + kBlockBarriers * 8 + 16 + 1024;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_block_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+                      BlockParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint16_t* out_tile = reinterpret_cast<uint16_t*>(smem + kBlockStages * kBlockStage);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBlockBarrierOffset);
+  uint64_t* full = bars;
+  uint64_t* ready = bars + kBlockStages;
+  uint64_t* empty = bars + 2 * kBlockStages;
+  uint64_t* acc_full = bars + 3 * kBlockStages;
+  uint64_t* final_bar = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBlockBarriers);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const uint32_t kblocks = (p.depth + kBK - 1) / kBK;
+  const uint32_t col_tile0 = blockIdx.x * 8;  // first 16-column tile of this CTA
+  const bool activate = p.activate != 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBlockStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_a);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      uint32_t stage = 0, phase = 0;
+      uint32_t last_parity[kBlockStages];
+      bool used[kBlockStages] = {false, false, false, false};
+      for (uint32_t kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, kWatchEmpty, abort_flag)) break;
+        uint8_t* w_dst = smem + stage * kBlockStage;
+        uint8_t* a_dst = w_dst + kBlockW;
+        mbar_arrive_expect_tx(&full[stage], kBlockStage);
+        tma_load_3d(w_dst, &tmap_w, &full[stage], 0, int32_t(kb * kBK), int32_t(col_tile0));
+        tma_load_3d(a_dst, &tmap_a, &full[stage], 0, 0, int32_t(kb * (kBK / 16)));
+        used[stage] = true;
+        last_parity[stage] = phase;
+        if (++stage == kBlockStages) { stage = 0; phase ^= 1u; }
+      }
+      for (int s = 0; s < kBlockStages; ++s)
+        if (used[s]) mbar_wait(&full[s], last_parity[s], kWatchFull, nullptr);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc_bf16(128, 32, 1, 0);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (uint32_t kb = 0; kb < kblocks; ++kb) {
+        uint64_t* wait_on = activate ? &ready[stage] : &full[stage];
+        if (!mbar_wait(wait_on, phase, kWatchFull, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t w_addr = smem_u32(smem + stage * kBlockStage);
+        const uint32_t a_addr = w_addr + kBlockW;
+#pragma unroll
+        for (uint32_t kk = 0; kk < kBK / 16; ++kk) {
+          // Weights: MN-major, 16-column groups 64 rows x 32 B apart (LBO), 8-row groups 256 B apart (SBO).
+          const uint64_t w_desc = make_smem_desc(w_addr + kk * 512, kBK * 32, 256, kLayoutSw32);
+          // Activations: K-major, one 16-deep tile (32 rows x 32 B) per MMA, 8-row groups 256 B apart.
+          const uint64_t a_desc = make_smem_desc(a_addr + kk * 1024, 16, 256, kLayoutSw32);
+          umma_bf16(tmem_base, w_desc, a_desc, idesc, (kb | kk) != 0u);
+        }
+        umma_commit(&empty[stage]);
+        if (++stage == kBlockStages) { stage = 0; phase ^= 1u; }
+      }
+      if (ok) umma_commit(acc_full);
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, kWatchOther, nullptr);
+    }
+  } else {
+    const uint32_t t128 = threadIdx.x - 64;  // 0..127
+    if (activate) {
+      // GELU on each staged activation tile (4096 bytes = 2048 values: 16 per thread), then release it to the MMA.
+      uint32_t stage = 0, phase = 0;
+      for (uint32_t kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&full[stage], phase, kWatchFull, abort_flag)) break;
+        uint4* a4 = reinterpret_cast<uint4*>(smem + stage * kBlockStage + kBlockW);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          uint4 w = a4[t128 * 2 + q];
+          uint32_t* ws = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+          for (int h = 0; h < 4; ++h) ws[h] = pack_bf16x2(gelu_erf(bf16_lo(ws[h])), gelu_erf(bf16_hi(ws[h])));
+          a4[t128 * 2 + q] = w;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&ready[stage]);
+        if (++stage == kBlockStages) { stage = 0; phase ^= 1u; }
+      }
+    }
+    // Epilogue: thread = output column (TMEM lane), 32 accumulator columns = the block's 32 tokens.
+    const uint32_t lane_base = 32u * (warp & 3u);
+    const uint32_t col = lane_base + lane;  // 0..127 within the CTA
+    const uint32_t col_global = col_tile0 * 16 + col;
+    if (mbar_wait(acc_full, 0, kWatchAccFull, abort_flag)) {
+      tc_fence_after();
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tmem_base + (lane_base << 16), r);
+      tmem_wait_ld();
+      const uint32_t ct = col >> 4, j = col & 15u;
+#pragma unroll
+      for (int t = 0; t < 32; ++t) {
+        float v = __uint_as_float(r[t]);
+        // Token t reads bias row t % 4 of its feature tile, as the broadcast read does (bf16.py:159-175).
+        if (p.bias != nullptr && col_global < p.columns)
+          v += bf16_to_float(p.bias[(size_t(col_tile0 + ct) * 4 + (t & 3)) * 16 + j]);
+        out_tile[(ct * 32 + t) * 16 + j] = float_to_bf16(v);
+      }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    // The CTA's 8 tiles are contiguous in the drain: 8 x 1 KB past the zero tile and the tiles before them.
+    const uint32_t tiles_valid = min(8u, p.columns / 16 - col_tile0);
+    uint4* dst = reinterpret_cast<uint4*>(p.drain + 256 + size_t(col_tile0) * 512);
+    const uint4* src = reinterpret_cast<const uint4*>(out_tile);
+    for (uint32_t i = t128; i < tiles_valid * 64; i += 128) dst[i] = src[i];
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 32);
+  }
+}
+
+template <int BN, int STAGES>
+tempo_status launch_rowmajor(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const RowMajorParams& base,
+                             cudaStream_t stream) {
+  using L = RowMajorSmem<BN, STAGES>;
+  CUtensorMap ta, tb;
+  const uint64_t a_dims[2] = {base.k, base.m};
+  const uint64_t a_strides[1] = {uint64_t(lda) * 2};
+  const uint32_t a_box[2] = {kBK, 128};
+  tempo_status s = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, a_dims, a_strides, a_box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != TEMPO_OK) return s;
+  const uint64_t b_dims[2] = {base.k, base.n};
+  const uint64_t b_strides[1] = {uint64_t(ldw) * 2};
+  const uint32_t b_box[2] = {kBK, uint32_t(BN)};
+  s = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_t, b_dims, b_strides, b_box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != TEMPO_OK) return s;
+  RowMajorParams p = base;
+  p.m_tiles = (p.m + 127) / 128;
+  p.n_tiles = (p.n + BN - 1) / BN;
+  const uint32_t tiles = p.m_tiles * p.n_tiles;
+  const uint32_t grid = tiles < uint32_t(sm_count()) ? tiles : uint32_t(sm_count());
+  auto kernel = gemm_rowmajor_kernel<BN, STAGES>;
+  s = set_smem(reinterpret_cast<const void*>(kernel), L::kBytes);
+  if (s != TEMPO_OK) return s;
+  kernel<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, p);
+  return check_launch("gemm_rowmajor_kernel");
+}
+
+}  // namespace
+
+}  // namespace tempo
+
+using namespace tempo;
+
+extern "C" tempo_status tempo_gemm(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
+                                   const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m,
+                                   uint32_t n, uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx,
+                                   void* stream) {
+  if (m == 0 || n == 0 || k == 0) return fail(TEMPO_ERR_VALUE, "tempo_gemm: empty problem %ux%ux%u", m, n, k);
+  if (k % 8 || lda % 8 || ldw % 8 || lda < k || ldw < k)
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm: K (%u) and the row strides (%u, %u) must be multiples of 8 and >= K", k,
+                lda, ldw);
+  if (!aligned16(a) || !aligned16(w_t)) return fail(TEMPO_ERR_VALUE, "tempo_gemm: operands must be 16-byte aligned");
+  const bool argmax = (flags & TEMPO_GEMM_ARGMAX) != 0;
+  if (argmax && (part_val == nullptr || part_idx == nullptr))
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm: argmax mode needs the partial buffers");
+  if (!argmax && (out == nullptr || ldo < n || (ldo % 8) || !aligned16(out)))
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm: output must be 16-byte aligned with a row stride >= N, multiple of 8");
+  if (residual != nullptr && (ldr < n || (ldr % 8) || !aligned16(residual)))
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm: residual must be 16-byte aligned with a row stride >= N, multiple of 8");
+  if (bias != nullptr && !aligned16(bias)) return fail(TEMPO_ERR_VALUE, "tempo_gemm: bias must be 16-byte aligned");
+  RowMajorParams p{};
+  p.bias = static_cast<const uint16_t*>(bias);
+  p.residual = static_cast<const uint16_t*>(residual);
+  p.out = static_cast<uint16_t*>(out);
+  p.part_val = part_val;
+  p.part_idx = part_idx;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.ldo = ldo;
+  p.ldr = ldr;
+  p.flags = flags;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (argmax) return launch_rowmajor<256, 4>(a, lda, w_t, ldw, p, st);
+  // Wide tiles when the grid still fills the GPU; narrower ones for the small-M decode GEMMs.
+  const uint64_t tiles256 = uint64_t((m + 127) / 128) * ((n + 255) / 256);
+  if (tiles256 >= uint64_t(sm_count())) return launch_rowmajor<256, 4>(a, lda, w_t, ldw, p, st);
+  const uint64_t tiles128 = uint64_t((m + 127) / 128) * ((n + 127) / 128);
+  if (tiles128 >= uint64_t(sm_count()) / 2) return launch_rowmajor<128, 6>(a, lda, w_t, ldw, p, st);
+  return launch_rowmajor<64, 8>(a, lda, w_t, ldw, p, st);
+}
+
+extern "C" tempo_status tempo_block_gemm(const void* activations, const void* weights, void* drain, const void* bias,
+                                         uint32_t depth, uint32_t columns, uint32_t activate, void* stream) {
+  if (depth == 0 || columns == 0 || depth % 16 || columns % 16)
+    return fail(TEMPO_ERR_VALUE, "tempo_block_gemm: depth (%u) and columns (%u) must be positive multiples of 16",
+                depth, columns);
+  if (!aligned16(activations) || !aligned16(weights) || !aligned16(drain) || (bias && !aligned16(bias)))
+    return fail(TEMPO_ERR_VALUE, "tempo_block_gemm: operands must be 16-byte aligned");
+  CUtensorMap tw, ta;
+  // Weights [columns/16][depth][16]: dims (16, depth, columns/16), box (16, 64, 8).
+  const uint64_t w_dims[3] = {16, depth, columns / 16};
+  const uint64_t w_strides[2] = {32, uint64_t(depth) * 32};
+  const uint32_t w_box[3] = {16, kBK, 8};
+  tempo_status s = encode_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, weights, w_dims, w_strides, w_box,
+                               CU_TENSOR_MAP_SWIZZLE_32B);
+  if (s != TEMPO_OK) return s;
+  // Activations [depth/16][32][16]: dims (16, 32, depth/16), box (16, 32, 4).
+  const uint64_t a_dims[3] = {16, 32, depth / 16};
+  const uint64_t a_strides[2] = {32, 1024};
+  const uint32_t a_box[3] = {16, 32, kBK / 16};
+  s = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, activations, a_dims, a_strides, a_box,
+                  CU_TENSOR_MAP_SWIZZLE_32B);
+  if (s != TEMPO_OK) return s;
+  BlockParams p{static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(drain), depth, columns, activate};
+  s = set_smem(reinterpret_cast<const void*>(gemm_block_kernel), kBlockSmem);
+  if (s != TEMPO_OK) return s;
+  const uint32_t grid = (columns / 16 + 7) / 8;
+  gemm_block_kernel<<<grid, kThreads, kBlockSmem, static_cast<cudaStream_t>(stream)>>>(tw, ta, p);
+  return check_launch("gemm_block_kernel");
+}

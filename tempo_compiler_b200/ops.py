@@ -1,0 +1,157 @@
+"""torch-tensor wrappers over the native C-ABI entry points (section 3 of include/tempo_b200.h).
+
+torch supplies device memory and the current CUDA stream; every op passes raw pointers and sizes to
+libtempo_b200.so, whose kernels do the work. Nothing here computes on its own, and nothing falls back: a CPU tensor,
+a wrong dtype or a missing library raises.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from tempo_compiler_b200 import lib as _lib
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _check(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor: the B200 kernels have no CPU path")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def gemm(a: torch.Tensor, w_t: torch.Tensor, *, bias: torch.Tensor | None = None,
+         residual: torch.Tensor | None = None, gelu: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M, N] = epilogue(a[M, K] @ w_t[N, K]^T): + bias, exact-erf GELU (of the BF16-rounded sum), + residual."""
+    _check(a, torch.bfloat16, "a")
+    _check(w_t, torch.bfloat16, "w_t")
+    m, k = a.shape
+    n = w_t.shape[0]
+    if w_t.shape[1] != k:
+        raise ValueError(f"inner dimensions differ: a {tuple(a.shape)}, w_t {tuple(w_t.shape)}")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+    _check(out, torch.bfloat16, "out")
+    if bias is not None:
+        _check(bias, torch.bfloat16, "bias")
+    if residual is not None:
+        _check(residual, torch.bfloat16, "residual")
+    flags = _lib.GEMM_GELU if gelu else 0
+    _lib.call("tempo_gemm", a.data_ptr(), k, w_t.data_ptr(), k, _ptr(bias), _ptr(residual), n, out.data_ptr(), n, m, n,
+              k, flags, None, None, _stream())
+    return out
+
+
+def gemm_argmax(a: torch.Tensor, w_t: torch.Tensor, part_val: torch.Tensor, part_idx: torch.Tensor) -> None:
+    """Per-row (max, first argmax) of a @ w_t^T over each 256-column tile into the partial buffers [M, ceil(N/256)]."""
+    _check(a, torch.bfloat16, "a")
+    _check(w_t, torch.bfloat16, "w_t")
+    m, k = a.shape
+    n = w_t.shape[0]
+    _lib.call("tempo_gemm", a.data_ptr(), k, w_t.data_ptr(), k, None, None, n, None, n, m, n, k, _lib.GEMM_ARGMAX,
+              part_val.data_ptr(), part_idx.data_ptr(), _stream())
+
+
+def argmax_finish(part_val: torch.Tensor, part_idx: torch.Tensor, ids: torch.Tensor, *,
+                  tokens_out: torch.Tensor | None = None, out_stride: int = 1, positions: torch.Tensor | None = None,
+                  advance: int = 0) -> None:
+    rows, tiles = part_val.shape
+    _lib.call("tempo_argmax_finish", part_val.data_ptr(), part_idx.data_ptr(), rows, tiles, ids.data_ptr(),
+              _ptr(tokens_out), out_stride, _ptr(positions), advance, _stream())
+
+
+def layernorm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, *, epsilon: float = 1e-5,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(x, torch.bfloat16, "x")
+    rows, features = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.call("tempo_layernorm", x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), out.data_ptr(), rows, features,
+              float(epsilon), _stream())
+    return out
+
+
+def embed(ids: torch.Tensor, positions: torch.Tensor, wte: torch.Tensor, wpe: torch.Tensor, *,
+          out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(ids, torch.int32, "ids")
+    _check(positions, torch.int32, "positions")
+    rows, width = ids.numel(), wte.shape[1]
+    if out is None:
+        out = torch.empty((rows, width), dtype=torch.bfloat16, device=wte.device)
+    _lib.call("tempo_embed", ids.data_ptr(), positions.data_ptr(), wte.data_ptr(), wpe.data_ptr(), out.data_ptr(), rows,
+              width, wte.shape[0], wpe.shape[0], _stream())
+    return out
+
+
+def attention_prefill(qkv: torch.Tensor, seqs: int, tokens: int, heads: int, *,
+                      out: torch.Tensor | None = None) -> torch.Tensor:
+    _check(qkv, torch.bfloat16, "qkv")
+    width = qkv.shape[1] // 3
+    if out is None:
+        out = torch.empty((seqs * tokens, width), dtype=torch.bfloat16, device=qkv.device)
+    _lib.call("tempo_attention_prefill", qkv.data_ptr(), out.data_ptr(), seqs, tokens, heads, width // heads, _stream())
+    return out
+
+
+def kv_store(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, seq_of: torch.Tensor,
+             pos_of: torch.Tensor) -> None:
+    seqs, heads, capacity, head = k_cache.shape
+    _lib.call("tempo_kv_store", qkv.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), seq_of.data_ptr(),
+              pos_of.data_ptr(), seq_of.numel(), seqs, heads, head, capacity, _stream())
+
+
+def decode_attention(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lengths: torch.Tensor, *,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    seqs, heads, capacity, head = k_cache.shape
+    if out is None:
+        out = torch.empty((seqs, heads * head), dtype=torch.bfloat16, device=qkv.device)
+    _lib.call("tempo_decode_attention", qkv.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), lengths.data_ptr(),
+              out.data_ptr(), seqs, heads, head, capacity, _stream())
+    return out
+
+
+# ---- the packed per-block ops on raw device tensors (uint16 words) ----
+
+def block_gemm(activations: torch.Tensor, weights: torch.Tensor, drain: torch.Tensor, bias: torch.Tensor | None,
+               depth: int, columns: int, activate: bool) -> None:
+    _lib.call("tempo_block_gemm", activations.data_ptr(), weights.data_ptr(), drain.data_ptr(), _ptr(bias), depth,
+              columns, int(activate), _stream())
+
+
+def block_add(left: torch.Tensor, right: torch.Tensor, out: torch.Tensor, features: int, broadcast: bool) -> None:
+    _lib.call("tempo_block_add", left.data_ptr(), right.data_ptr(), out.data_ptr(), features, int(broadcast), _stream())
+
+
+def block_layernorm(rows: torch.Tensor, constants: torch.Tensor, out: torch.Tensor, features: int) -> None:
+    _lib.call("tempo_block_layernorm", rows.data_ptr(), constants.data_ptr(), out.data_ptr(), features, _stream())
+
+
+def block_attention(constants: torch.Tensor, fused_operand: int, tokens: int, heads: int) -> None:
+    _lib.call("tempo_block_attention", constants.data_ptr(), fused_operand, tokens, heads, 64, _stream())
+
+
+def block_decode_attention(constants: torch.Tensor, cache_operand: int, fused_operand: int, keys: int, heads: int,
+                           stated: int = 0) -> None:
+    _lib.call("tempo_block_decode_attention", constants.data_ptr(), cache_operand, fused_operand, keys, heads, 64,
+              stated, _stream())
+
+
+def block_copy(source: int, destination: int, rows: int, stride: int) -> None:
+    _lib.call("tempo_block_copy", source, destination, rows, stride, _stream())
+
+
+def watchdog() -> int:
+    """Reads and clears the kernels' bounded-wait watchdog (0 = no wait expired)."""
+    import ctypes
+    code = ctypes.c_int32()
+    _lib.call("tempo_watchdog", ctypes.byref(code))
+    return int(code.value)

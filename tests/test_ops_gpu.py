@@ -1,0 +1,324 @@
+"""Per-op parity of the B200 kernels against the oracle, through the C ABI.
+
+Tolerances are the reference's own: GEMM rel-Frobenius < 1e-2 vs float64 and exact on structured operands
+(board_package/board_checks.py:227-248), add exact (:285-288), LayerNorm < 2% vs the device model (:335-359),
+causal attention < 2% and decode < 2-3% vs float64 (tests/test_mlir_attention.py:227,246), KV copies exact.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from oracle import bf16 as ob
+from oracle import references as orf
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _device():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from tempo_compiler_b200 import lib
+    lib.load()
+    yield
+    from tempo_compiler_b200 import ops
+    torch.cuda.synchronize()
+    assert ops.watchdog() == 0
+
+
+def _words(array_u16: np.ndarray) -> "torch.Tensor":
+    return torch.from_numpy(np.ascontiguousarray(array_u16).view(np.int16)).cuda()
+
+
+def _host(tensor) -> np.ndarray:
+    return tensor.cpu().numpy().view(np.uint16)
+
+
+def _bf16(values) -> "torch.Tensor":
+    return torch.from_numpy(np.ascontiguousarray(values, np.float32)).cuda().to(torch.bfloat16)
+
+
+def _packed_block(rows: np.ndarray) -> np.ndarray:
+    """A packed device block: 512-byte zero tile then [features/16][32][16] words."""
+    return np.concatenate([np.zeros(256, np.uint16), ob.pack_activations(rows)])
+
+
+# ------------------------------------------------------------------------------------------------------------
+# add / add_bias / layernorm / copy on the packed layout
+# ------------------------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize("features", [128, 768, 2304, 3072])
+@pytest.mark.parametrize("broadcast", [False, True])
+def test_block_add_is_exact(features: int, broadcast: bool) -> None:
+    from tempo_compiler_b200 import ops
+    rng = np.random.default_rng(features + broadcast)
+    left = ob.bf16_grid(rng.standard_normal((32, features)).astype(np.float32))
+    right = ob.bf16_grid(rng.standard_normal(features if broadcast else (32, features)).astype(np.float32))
+    d_left = _words(ob.pack_activations(left))
+    d_right = _words(ob.pack_bias(right) if broadcast else ob.pack_activations(right))
+    d_out = torch.zeros_like(d_left)
+    ops.block_add(d_left, d_right, d_out, features, broadcast)
+    got = ob.unpack_activations(_host(d_out), tokens=32, features=features)
+    np.testing.assert_array_equal(got, ob.bf16_grid(left + right))
+
+
+def test_block_layernorm_matches_device_model() -> None:
+    from tempo_compiler_b200 import ops
+    rng = np.random.default_rng(0)
+    rows = ob.bf16_grid((rng.standard_normal((32, 768)) * 2.0).astype(np.float32))
+    gamma = ob.bf16_grid((1.0 + 0.1 * rng.standard_normal(768)).astype(np.float32))
+    beta = ob.bf16_grid((0.1 * rng.standard_normal(768)).astype(np.float32))
+    constants = ob.bf16_bits(np.concatenate([gamma, beta, np.full(64, 1 / 768, np.float32),
+                                             np.full(64, 9.999999747378752e-06, np.float32)]))
+    d_rows = _words(ob.pack_activations(rows))
+    d_out = torch.zeros_like(d_rows)
+    ops.block_layernorm(d_rows, _words(constants), d_out, 768)
+    got = ob.unpack_activations(_host(d_out), tokens=32, features=768)
+    assert orf.relative_error(got, orf.layernorm_device(rows, gamma, beta)) < 0.02
+    assert orf.relative_error(got, orf.layernorm_f64(rows, gamma, beta)) < 0.005
+
+
+@pytest.mark.parametrize(("rows", "stride"), [(1, 32), (96, 1024), (129, 32), (300, 64), (3072, 32)])
+def test_block_copy_moves_exactly_the_rows(rows: int, stride: int) -> None:
+    from tempo_compiler_b200 import ops
+    span = rows * stride
+    source = np.random.default_rng(rows + stride).integers(0, 1 << 16, span // 2, dtype=np.uint16)
+    d_src = _words(source)
+    d_dst = torch.zeros_like(d_src)
+    ops.block_copy(d_src.data_ptr(), d_dst.data_ptr(), rows, stride)
+    got = _host(d_dst)
+    moved = np.zeros(span // 2, dtype=bool)
+    for row in range(rows):
+        moved[row * stride // 2: row * stride // 2 + 16] = True
+    np.testing.assert_array_equal(got[moved], source[moved])
+    assert not got[~moved].any()
+
+
+# ------------------------------------------------------------------------------------------------------------
+# the packed per-block GEMM (tcgen05, swap-AB)
+# ------------------------------------------------------------------------------------------------------------
+
+def _run_block_gemm(left, right, bias, activate):
+    from tempo_compiler_b200 import ops
+    depth, columns = right.shape
+    d_act = _words(ob.pack_activations(left))
+    d_w = _words(ob.pack_weights(right))
+    d_bias = _words(ob.pack_bias(bias)) if bias is not None else None
+    d_drain = torch.zeros(256 + columns * 32, dtype=torch.int16, device="cuda")
+    ops.block_gemm(d_act, d_w, d_drain, d_bias, depth, columns, activate)
+    torch.cuda.synchronize()
+    words = _host(d_drain)
+    assert not words[:256].any(), "the clearing tile must stay zero"
+    return ob.unpack_activations(words[256:], tokens=32, features=columns)
+
+
+def test_block_gemm_structured_operands_are_exact() -> None:
+    left, right = ob.build_operands(32, 768, 3072, kind="structured", seed=0)
+    np.testing.assert_array_equal(_run_block_gemm(left, right, None, False), (left @ right).astype(np.float32))
+
+
+@pytest.mark.parametrize(("depth", "columns"), [(768, 3072), (768, 768), (768, 2304), (3072, 768), (64, 16),
+                                                (96, 48), (4112, 48)])
+def test_block_gemm_varying_operands_within_one_percent(depth: int, columns: int) -> None:
+    left, right = ob.build_operands(32, depth, columns, kind="varying", seed=0)
+    error = orf.relative_error(_run_block_gemm(left, right, None, False), orf.gemm_f64(left, right))
+    assert error < 0.01, error
+
+
+@pytest.mark.parametrize(("depth", "columns", "activate"), [(768, 768, False), (3072, 768, True), (768, 3072, True)])
+def test_block_gemm_folds_bias_and_gelu(depth: int, columns: int, activate: bool) -> None:
+    left, right = ob.build_operands(32, depth, columns, kind="varying", seed=0)
+    right = ob.bf16_grid(right * np.float32(0.02))
+    bias = ob.bf16_grid(np.random.default_rng(1).standard_normal(columns).astype(np.float32))
+    expected = orf.gemm_f64(left, right, bias=bias, activate=activate)
+    error = orf.relative_error(_run_block_gemm(left, right, bias, activate), expected)
+    assert error < 0.01, error
+
+
+def test_block_gemm_deep_contraction_is_exact() -> None:
+    """Sparse small-integer operands whose every partial sum BF16 holds: any dropped or repeated k-tile shows
+    (tests/test_mlir_padding.py:208-221)."""
+    rng = np.random.default_rng(3)
+    depth, columns = 4112, 48
+    left = ((rng.random((32, depth)) < 16 / depth) * rng.choice([1.0, 2.0], (32, depth))).astype(np.float32)
+    right = rng.choice([-1.0, 0.5, 1.0], (depth, columns)).astype(np.float32)
+    offsets = rng.integers(-4, 4, columns).astype(np.float32)
+    np.testing.assert_array_equal(_run_block_gemm(left, right, offsets, False), left @ right + offsets)
+
+
+# ------------------------------------------------------------------------------------------------------------
+# the native row-major GEMM (tcgen05, persistent, double-buffered accumulators)
+# ------------------------------------------------------------------------------------------------------------
+
+@pytest.mark.parametrize(("m", "n", "k"), [(128, 256, 64), (1024, 2304, 768), (1000, 768, 768), (512, 3072, 768),
+                                           (64, 768, 3072), (300, 200, 136), (4096, 768, 3072)])
+@pytest.mark.parametrize("epilogue", ["plain", "bias", "gelu", "residual"])
+def test_gemm_matches_fp32_reference(m: int, n: int, k: int, epilogue: str) -> None:
+    from tempo_compiler_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
+    a = torch.randn((m, k), generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn((n, k), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=g, device="cuda") * 0.1).to(torch.bfloat16) if epilogue != "plain" else None
+    residual = torch.randn((m, n), generator=g, device="cuda").to(torch.bfloat16) if epilogue == "residual" else None
+    out = ops.gemm(a, w, bias=bias, residual=residual, gelu=epilogue == "gelu")
+    ref = a.float() @ w.float().T
+    if bias is not None:
+        ref = ref + bias.float()
+    if epilogue == "gelu":
+        ref = torch.nn.functional.gelu(ref.to(torch.bfloat16).float())
+    if residual is not None:
+        ref = ref + residual.float()
+    error = ((out.float() - ref).norm() / ref.norm()).item()
+    assert error < 5e-3, error
+    assert torch.isfinite(out.float()).all()
+
+
+def test_gemm_argmax_matches_torch() -> None:
+    from tempo_compiler_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randn((200, 768), generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn((50257, 768), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    tiles = (50257 + 255) // 256
+    part_val = torch.empty((200, tiles), dtype=torch.float32, device="cuda")
+    part_idx = torch.empty((200, tiles), dtype=torch.int32, device="cuda")
+    ids = torch.empty(200, dtype=torch.int32, device="cuda")
+    ops.gemm_argmax(a, w, part_val, part_idx)
+    ops.argmax_finish(part_val, part_idx, ids)
+    logits = a.float() @ w.float().T
+    expected = logits.argmax(dim=1).to(torch.int32)
+    top2 = logits.topk(2, dim=1).values
+    clear = (top2[:, 0] - top2[:, 1]) > 1e-3
+    assert torch.equal(ids[clear], expected[clear])
+    assert clear.float().mean().item() > 0.9
+
+
+# ------------------------------------------------------------------------------------------------------------
+# attention
+# ------------------------------------------------------------------------------------------------------------
+
+def _fused_packed(fused: np.ndarray) -> np.ndarray:
+    """A packed fused QKV tensor: per 32-token block a zero tile and its [144][32][16] tiles."""
+    blocks = [_packed_block(fused[b * 32:(b + 1) * 32]) for b in range(fused.shape[0] // 32)]
+    return np.concatenate(blocks)
+
+
+def _unpack_fused(words: np.ndarray, tokens: int, features: int) -> np.ndarray:
+    per = 256 + 32 * features
+    return np.concatenate([ob.unpack_activations(words[b * per + 256:(b + 1) * per], tokens=32, features=features)
+                           for b in range(tokens // 32)])
+
+
+@pytest.mark.parametrize("tokens", [32, 64, 160, 256, 1024])
+def test_block_causal_attention_within_two_percent(tokens: int) -> None:
+    from tempo_compiler_b200 import ops
+    rng = np.random.default_rng(tokens)
+    fused = ob.bf16_grid(rng.standard_normal((tokens, 3 * 768)).astype(np.float32))
+    fused[:, :768] = ob.bf16_grid(fused[:, :768] / 8.0)  # the queries arrive scaled by 1/sqrt(64)
+    d_fused = _words(_fused_packed(fused))
+    constants = _words(ob.causal_constants_words())
+    ops.block_attention(constants, d_fused.data_ptr() + 512, tokens, 12)
+    got = _unpack_fused(_host(d_fused), tokens, 3 * 768)
+    np.testing.assert_array_equal(got[:, 768:], fused[:, 768:])  # keys and values untouched
+    for h in range(12):
+        cols = slice(h * 64, (h + 1) * 64)
+        expected = orf.causal_attention_f64(fused[:, cols], fused[:, 768:][:, cols], fused[:, 1536:][:, cols])
+        error = orf.relative_error(got[:, cols], expected)
+        assert error < 0.02, (h, error)
+
+
+@pytest.mark.parametrize(("seqs", "tokens"), [(1, 64), (2, 200), (3, 128), (1, 1024), (4, 384)])
+def test_native_prefill_attention_matches_fp32(seqs: int, tokens: int) -> None:
+    from tempo_compiler_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(seqs * 1000 + tokens)
+    qkv = torch.randn((seqs * tokens, 3 * 768), generator=g, device="cuda").to(torch.bfloat16)
+    qkv[:, :768] = (qkv[:, :768].float() / 8.0).to(torch.bfloat16)
+    out = ops.attention_prefill(qkv, seqs, tokens, 12)
+    q = qkv[:, :768].float().view(seqs, tokens, 12, 64).transpose(1, 2)
+    k = qkv[:, 768:1536].float().view(seqs, tokens, 12, 64).transpose(1, 2)
+    v = qkv[:, 1536:].float().view(seqs, tokens, 12, 64).transpose(1, 2)
+    ref = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True, scale=1.0)
+    ref = ref.transpose(1, 2).reshape(seqs * tokens, 768)
+    error = ((out.float() - ref).norm() / ref.norm()).item()
+    assert error < 0.01, error
+
+
+@pytest.mark.parametrize(("keys", "length"), [(64, 1), (64, 49), (256, 200), (1024, 1024)])
+def test_block_decode_attention_matches_float64(keys: int, length: int) -> None:
+    from tempo_compiler_b200 import ops
+    rng = np.random.default_rng(keys + length)
+    fused = ob.bf16_grid(rng.standard_normal((32, 3 * 768)).astype(np.float32))
+    cache = ob.bf16_grid(rng.standard_normal((keys, 2 * 768)).astype(np.float32))
+    masks = ob.decode_mask_tiles(keys=keys, length=length)
+    constants = ob.pack_attention_constants(initial_maximum=-1e30, constants=(),
+                                            masks=np.ascontiguousarray(masks.swapaxes(-1, -2))).reshape(-1)
+    d_fused = _words(_fused_packed(fused))
+    d_cache = _words(_fused_packed_cache(cache))
+    ops.block_decode_attention(_words(constants), d_cache.data_ptr() + 512, d_fused.data_ptr() + 512, keys, 12)
+    got = _unpack_fused(_host(d_fused), 32, 3 * 768)
+    expected = np.concatenate([orf.attention_f64(fused[:1, h * 64:(h + 1) * 64], cache[:length, h * 64:(h + 1) * 64],
+                                                 cache[:length, 768 + h * 64:768 + (h + 1) * 64])
+                               for h in range(12)], axis=1)[0]
+    assert orf.relative_error(got[0, :768], expected) < (0.03 if keys > 256 else 0.02)
+    np.testing.assert_array_equal(got[16:], fused[16:])  # only the first 16 query rows are written
+
+
+def _fused_packed_cache(cache: np.ndarray) -> np.ndarray:
+    return np.concatenate([_packed_block(cache[b * 32:(b + 1) * 32]) for b in range(cache.shape[0] // 32)])
+
+
+@pytest.mark.parametrize(("seqs", "capacity", "lengths"), [(3, 64, (1, 33, 64)), (2, 1152, (1024, 1100))])
+def test_native_decode_attention_matches_fp32(seqs: int, capacity: int, lengths) -> None:
+    from tempo_compiler_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(capacity)
+    qkv = torch.randn((seqs, 3 * 768), generator=g, device="cuda").to(torch.bfloat16)
+    kc = torch.randn((seqs, 12, capacity, 64), generator=g, device="cuda").to(torch.bfloat16)
+    vc = torch.randn((seqs, 12, capacity, 64), generator=g, device="cuda").to(torch.bfloat16)
+    lens = torch.tensor(lengths, dtype=torch.int32, device="cuda")
+    out = ops.decode_attention(qkv, kc, vc, lens)
+    for s, length in enumerate(lengths):
+        q = qkv[s, :768].float().view(12, 1, 64)
+        scores = q @ kc[s, :, :length].float().transpose(1, 2)
+        ref = (scores.softmax(-1) @ vc[s, :, :length].float()).reshape(768)
+        error = ((out[s].float() - ref).norm() / ref.norm()).item()
+        assert error < 0.01, (s, error)
+
+
+# ------------------------------------------------------------------------------------------------------------
+# native LayerNorm, embedding, KV store
+# ------------------------------------------------------------------------------------------------------------
+
+def test_native_layernorm_matches_float64() -> None:
+    from tempo_compiler_b200 import ops
+    rng = np.random.default_rng(2)
+    rows = ob.bf16_grid((rng.standard_normal((1000, 768)) * 2.0 + 0.5).astype(np.float32))
+    gamma = ob.bf16_grid((1.0 + 0.1 * rng.standard_normal(768)).astype(np.float32))
+    beta = ob.bf16_grid((0.1 * rng.standard_normal(768)).astype(np.float32))
+    out = ops.layernorm(_bf16(rows), _bf16(gamma), _bf16(beta))
+    assert orf.relative_error(out.float().cpu().numpy(), orf.layernorm_f64(rows, gamma, beta)) < 0.005
+
+
+def test_embed_and_kv_store_are_exact() -> None:
+    from tempo_compiler_b200 import ops
+    rng = np.random.default_rng(4)
+    wte = ob.bf16_grid((rng.standard_normal((1000, 768)) * 0.02).astype(np.float32))
+    wpe = ob.bf16_grid((rng.standard_normal((64, 768)) * 0.02).astype(np.float32))
+    ids = rng.integers(0, 1000, 40).astype(np.int32)
+    pos = rng.integers(0, 64, 40).astype(np.int32)
+    x = ops.embed(torch.from_numpy(ids).cuda(), torch.from_numpy(pos).cuda(), _bf16(wte), _bf16(wpe))
+    np.testing.assert_array_equal(x.float().cpu().numpy(), ob.bf16_grid(wte[ids] + wpe[pos]))
+    qkv = torch.randn((40, 2304), device="cuda").to(torch.bfloat16)
+    kc = torch.zeros((4, 12, 16, 64), dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    seq_of = torch.arange(40, dtype=torch.int32, device="cuda") % 4
+    pos_of = torch.arange(40, dtype=torch.int32, device="cuda") // 4
+    ops.kv_store(qkv, kc, vc, seq_of, pos_of)
+    for r in range(40):
+        s, p = r % 4, r // 4
+        assert torch.equal(kc[s, :, p].reshape(768), qkv[r, 768:1536])
+        assert torch.equal(vc[s, :, p].reshape(768), qkv[r, 1536:])
