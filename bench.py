@@ -1,0 +1,359 @@
+#!/usr/bin/env python3
+"""GPT-2 small batched prefill + greedy-decode throughput on B200, one process per GPU.
+
+Workload (the batched throughput configuration): 512 independent sequences, each a 1024-token prefill followed by
+128 greedy decode steps, seeded uniform token ids and random-init weights ~N(0, 0.02). Sequences are sharded
+contiguously over the ranks (strong scaling: the job is fixed, each rank takes 512/N sequences); no collective is on
+the data path, the process group only times (barrier, max over ranks). One step = the whole job once.
+
+    python bench.py [--gpus N --steps K --warmup W]                      # the B200 arm
+    python bench.py --impl reference [--steps K --warmup W]              # the reference's CPU path (oracle port)
+
+Prints one JSON line on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+METRIC = "GPT-2-small prefill+decode tok/s at 1/2/4/8 B200; GEMM % of bf16 TC peak"
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse() -> argparse.Namespace:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--sequences", type=int, default=512)
+    p.add_argument("--prompt", type=int, default=1024)
+    p.add_argument("--decode", type=int, default=128)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--cpu-prompt", type=int, default=512, help="prompt of the bounded CPU sample")
+    p.add_argument("--cpu-decode", type=int, default=8, help="decode steps of the bounded CPU sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-graph", action="store_true", help="eager decode instead of the captured CUDA graph")
+    return p.parse_args()
+
+
+def peaks() -> tuple[dict, str]:
+    try:
+        with open(PEAKS_FILE) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def workload(args) -> dict:
+    return {"workload": (f"batched GPT-2 small: {args.sequences} sequences x ({args.prompt}-token prefill + "
+                         f"{args.decode} greedy decode steps)"),
+            "sequences": args.sequences, "prompt_tokens": args.prompt, "decode_steps": args.decode,
+            "parallelism": f"sequences sharded over {args.gpus} GPU(s), no collective on the data path",
+            "l2": "inputs larger than L2 (170 MB weights + the KV cache, 21.7 GB at 512 sequences)"}
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# CPU side: the reference's own host path (the oracle's restatement of board_package/references.py)
+# ---------------------------------------------------------------------------------------------------------------
+
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        counts = [info.get("num_threads", 1) for info in threadpool_info() if info.get("user_api") == "blas"]
+        return max(counts) if counts else 1
+    except Exception:  # noqa: BLE001
+        return 1
+
+
+def cpu_sample(args, layers, shared) -> tuple[float, int]:
+    """Runs one bounded sample of the workload on the host: one sequence, a `cpu_prompt`-token prefill and
+    `cpu_decode` greedy steps through the reference's device-rounding host references (KV-cached chain built from
+    them). Returns (seconds, tokens processed)."""
+    from oracle.model import CachedChain
+    from tempo_compiler_b200.weights import random_token_ids
+    ids = [int(t) for t in random_token_ids(args.seed + 1000, args.cpu_prompt)]
+    chain = CachedChain(layers, shared, mode="device")
+    started = time.perf_counter()
+    chain.generate(ids, new_tokens=args.cpu_decode + 1)
+    return time.perf_counter() - started, args.cpu_prompt + args.cpu_decode
+
+
+def reference_arm(args) -> int:
+    if int(os.environ.get("RANK", "0")) != 0:
+        return 0
+    from tempo_compiler_b200.weights import random_gpt2
+    layers, shared = random_gpt2(args.seed)
+    for _ in range(args.warmup):
+        cpu_sample(args, layers, shared)
+    seconds, tokens = 0.0, 0
+    for _ in range(args.steps):
+        s, t = cpu_sample(args, layers, shared)
+        seconds += s
+        tokens += t
+    value = tokens / seconds
+    sample = (f"1 sequence: {args.cpu_prompt}-token prefill + {args.cpu_decode} greedy decode steps per step, "
+              f"numpy float64/BF16-rounding host references (board_package/references.py semantics)")
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * seconds / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16 storage, float64/BF16-rounded arithmetic",
+            "data": "synthetic (seeded uniform token ids, random-init weights ~N(0,0.02))", "config": workload(args),
+            "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Clock sampling during the timed region
+# ---------------------------------------------------------------------------------------------------------------
+
+class Clocks:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self) -> "Clocks":
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.index)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, value in zip(names, parts[5:9]):
+                if value.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# The B200 arm
+# ---------------------------------------------------------------------------------------------------------------
+
+def b200_arm(args) -> int:
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        args.gpus = world
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(value: float) -> float:
+        if world == 1:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    from tempo_compiler_b200 import lib, ops
+    from tempo_compiler_b200.engine import Engine
+    from tempo_compiler_b200.weights import random_gpt2, random_token_ids
+
+    lib.load()
+    layers, shared = random_gpt2(args.seed)
+    per_rank = args.sequences // world
+    if per_rank * world != args.sequences:
+        raise SystemExit(f"{args.sequences} sequences do not shard evenly over {world} ranks")
+    first = rank * per_rank
+    ids = np.stack([random_token_ids(args.seed + 1000 + s, args.prompt) for s in range(first, first + per_rank)])
+    ids = ids.astype(np.int32)
+    engine = Engine(layers, shared, batch=per_rank, prompt=args.prompt, capacity=args.prompt + args.decode,
+                    device=device)
+    ids_dev = torch.from_numpy(ids).to(device)
+    graph = not args.no_graph
+
+    # launch count of one step, from an eager run (the graph replays the same kernels)
+    ops.reset_launch_count()
+    engine.run(ids_dev, args.decode, graph=False)
+    torch.cuda.synchronize()
+    launches_per_step = ops.launch_count()
+
+    for _ in range(args.warmup):
+        engine.run(ids_dev, args.decode, graph=graph)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local).start()
+    start.record(stream)
+    for _ in range(args.steps):
+        engine.run(ids_dev, args.decode, graph=graph)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clock_info = clocks.stop()
+    ms = max_over_ranks(start.elapsed_time(end))
+    tokens_per_step = args.sequences * (args.prompt + args.decode)
+    value = tokens_per_step * args.steps / (ms / 1000.0)
+
+    # end to end through the public call: host prompts in (pinned), host tokens out
+    e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e2e_start.record(stream)
+    for _ in range(args.steps):
+        tokens = engine.generate(ids, args.decode, graph=graph)
+    e2e_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end))
+    e2e_value = tokens_per_step * args.steps / (e2e_ms / 1000.0)
+    h2d = args.sequences * args.prompt * 4
+    d2h = args.sequences * (args.decode + 1) * 4
+
+    # phase split and per-kernel rooflines, timed with CUDA events on the launching stream
+    measured, source = peaks()
+    prefill_ms = _time(lambda: engine.prefill(ids_dev), stream, 2)
+    decode_ms = _time(lambda: engine.decode(args.decode, graph=graph), stream, 1) if args.decode else 0.0
+    roof = _decode_attention_roofline(engine, stream, measured, source)
+    gemm_roof = _gemm_roofline(engine, stream, measured, source)
+    watchdog = ops.watchdog()
+
+    line = None
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded uniform token ids, random-init weights ~N(0,0.02))",
+                "config": workload(args),
+                "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "gpu_launches": launches_per_step * args.steps * world,
+                "clocks": clock_info, "roofline": roof, "gemm_roofline": gemm_roof,
+                "phases_ms_rank0": {"prefill": prefill_ms, "decode": decode_ms},
+                "decode_graph": graph, "watchdog": watchdog,
+                "tokens_checksum": int(np.asarray(tokens, dtype=np.int64).sum())}
+        if world == 1 and not args.no_cpu_baseline:
+            seconds, count = cpu_sample(args, layers, shared)
+            line["cpu_baseline"] = {
+                "value": count / seconds, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
+                "sample": (f"1 sequence: {args.cpu_prompt}-token prefill + {args.cpu_decode} greedy decode steps, "
+                           f"numpy host references (board_package/references.py semantics), {seconds:.1f} s")}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def _time(fn, stream, repeats: int) -> float:
+    import torch
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(repeats):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / repeats
+
+
+def _decode_attention_roofline(engine, stream, measured, source) -> dict:
+    """Decode attention over the full caches (every sequence at `capacity` keys): algorithmic bytes are each cached
+    key and value read once plus the query read and the output written."""
+    import torch
+    from tempo_compiler_b200 import ops
+    layer = len(engine.layers) // 2
+    lengths = torch.full((engine.batch,), engine.capacity, dtype=torch.int32, device=engine.device)
+    fn = lambda: ops.decode_attention(engine.dqkv, engine.k_cache[layer], engine.v_cache[layer], lengths,  # noqa
+                                      out=engine.dattn)
+    fn()
+    ms = _time(fn, stream, 20)
+    heads, head = engine.shape.heads, engine.shape.head
+    algorithmic = engine.batch * heads * engine.capacity * head * 2 * 2 + engine.batch * 3 * heads * head * 2 + \
+        engine.batch * heads * head * 2
+    achieved = algorithmic / (ms / 1000.0) / 1e9
+    peak = float(measured["hbm_gbs"])
+    return {"kernel": "decode_attention_kernel", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "traffic": None, "algorithmic_bytes_per_launch": algorithmic,
+            "launch_ms": ms, "peak_source": f"{source} ({PEAKS_FILE if source == 'measured' else 'fallback'})"}
+
+
+def _gemm_roofline(engine, stream, measured, source) -> dict:
+    """The prefill FC projection: M = sequences x prompt, N = 3072, K = 768, bias + exact-erf GELU epilogue."""
+    from tempo_compiler_b200 import ops
+    lw = engine.layers[0]
+    fn = lambda: ops.gemm(engine.ln, lw.w_fc, bias=lw.b_fc, gelu=True, out=engine.h)  # noqa: E731
+    fn()
+    ms = _time(fn, stream, 5)
+    m, k = engine.ln.shape
+    n = lw.w_fc.shape[0]
+    achieved = 2.0 * m * n * k / (ms / 1000.0) / 1e12
+    peak = float(measured["bf16_tflops"])
+    return {"kernel": "gemm_rowmajor_kernel (prefill FC, M=%d N=%d K=%d)" % (m, n, k), "bound": "tensor",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "launch_ms": ms,
+            "peak_source": f"{source} burst cuBLAS bf16"}
+
+
+def main() -> int:
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    return b200_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -171,9 +171,10 @@ tempo_status tempo_gemm(const void* a, uint32_t lda, const void* w_t, uint32_t l
                         const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m, uint32_t n,
                         uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx, void* stream);
 
-/* Row-wise LayerNorm of [rows, features] BF16 (features % 8 == 0, <= 4096), FP32 statistics, BF16 out. */
-tempo_status tempo_layernorm(const void* x, const void* gamma, const void* beta, void* out, uint32_t rows,
-                             uint32_t features, float epsilon, void* stream);
+/* Row-wise LayerNorm of `rows` BF16 rows of `features` (features % 8 == 0, <= 4096) read `x_stride` elements apart
+ * (x_stride % 8 == 0), FP32 statistics, BF16 out [rows, features]. */
+tempo_status tempo_layernorm(const void* x, uint32_t x_stride, const void* gamma, const void* beta, void* out,
+                             uint32_t rows, uint32_t features, float epsilon, void* stream);
 
 /* x[r] = round_bf16(wte[ids[r]] + wpe[positions[r]]) for r < rows; ids/positions int32 on the device. A row whose
  * id is outside [0, vocab) or position outside [0, max_positions) is written as zeros. */
@@ -192,17 +193,19 @@ tempo_status tempo_kv_store(const void* qkv, void* k_cache, void* v_cache, const
                             const int32_t* pos_of, uint32_t rows, uint32_t seqs, uint32_t heads, uint32_t head,
                             uint32_t capacity, void* stream);
 
-/* One query per sequence (row s of qkv, scaled) over the first lengths[s] cached keys of each head; out: [seqs,
- * heads*head] BF16. */
+/* One query per sequence (row s of qkv, scaled) over the first lengths[s] + length_offset cached keys of each head
+ * (clamped to [0, capacity]); out: [seqs, heads*head] BF16. */
 tempo_status tempo_decode_attention(const void* qkv, const void* k_cache, const void* v_cache,
-                                    const int32_t* lengths, void* out, uint32_t seqs, uint32_t heads, uint32_t head,
-                                    uint32_t capacity, void* stream);
+                                    const int32_t* lengths, int32_t length_offset, void* out, uint32_t seqs,
+                                    uint32_t heads, uint32_t head, uint32_t capacity, void* stream);
 
-/* Reduces argmax partials [rows][tiles] to token ids: ids[r] = first index of the row maximum; also writes ids to
- * tokens_out[r * out_stride] when tokens_out is not NULL, and advances positions[r] by `advance`. */
+/* Reduces argmax partials [rows][tiles] to token ids: ids[r] = first index of the row maximum (ties go to the lower
+ * index, as numpy's argmax). When tokens_out is not NULL the id is also written to tokens_out[r * out_stride + c] with
+ * c = positions[r] + index_offset (c = index_offset without positions), skipped unless 0 <= c < out_stride; then
+ * positions[r] advances by `advance`. Keeping the column on the device lets one captured decode step be replayed. */
 tempo_status tempo_argmax_finish(const float* part_val, const int32_t* part_idx, uint32_t rows, uint32_t tiles,
                                  int32_t* ids, int32_t* tokens_out, uint32_t out_stride, int32_t* positions,
-                                 int32_t advance, void* stream);
+                                 int32_t index_offset, int32_t advance, void* stream);
 
 #ifdef __cplusplus
 }

@@ -379,13 +379,13 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* _
                                                                const uint16_t* __restrict__ k_cache,
                                                                const uint16_t* __restrict__ v_cache,
                                                                const int32_t* __restrict__ lengths,
-                                                               uint16_t* __restrict__ out, uint32_t heads,
-                                                               uint32_t capacity) {
+                                                               int32_t length_offset, uint16_t* __restrict__ out,
+                                                               uint32_t heads, uint32_t capacity) {
   const uint32_t h = blockIdx.x, s = blockIdx.y;
   const uint32_t warp = warp_id(), lane = lane_id();
   const uint32_t g = lane >> 3, li = lane & 7u;
   const uint32_t width = heads * 64;
-  const int32_t len = min(lengths[s], int32_t(capacity));
+  const int32_t len = max(0, min(lengths[s] + length_offset, int32_t(capacity)));
   float q[8];
   load8(reinterpret_cast<const uint4*>(qkv + size_t(s) * 3 * width + h * 64)[li], q);
 #pragma unroll
@@ -575,8 +575,9 @@ extern "C" tempo_status tempo_block_decode_attention(const void* constants, cons
 }
 
 extern "C" tempo_status tempo_decode_attention(const void* qkv, const void* k_cache, const void* v_cache,
-                                               const int32_t* lengths, void* out, uint32_t seqs, uint32_t heads,
-                                               uint32_t head, uint32_t capacity, void* stream) {
+                                               const int32_t* lengths, int32_t length_offset, void* out,
+                                               uint32_t seqs, uint32_t heads, uint32_t head, uint32_t capacity,
+                                               void* stream) {
   if (seqs == 0 || heads == 0 || head != 64 || capacity == 0)
     return fail(TEMPO_ERR_VALUE, "tempo_decode_attention: seqs %u heads %u head %u capacity %u", seqs, heads, head,
                 capacity);
@@ -584,6 +585,6 @@ extern "C" tempo_status tempo_decode_attention(const void* qkv, const void* k_ca
     return fail(TEMPO_ERR_VALUE, "tempo_decode_attention: operands must be 16-byte aligned");
   decode_attention_kernel<<<dim3(heads, seqs), 128, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(qkv), static_cast<const uint16_t*>(k_cache), static_cast<const uint16_t*>(v_cache),
-      lengths, static_cast<uint16_t*>(out), heads, capacity);
+      lengths, length_offset, static_cast<uint16_t*>(out), heads, capacity);
   return check_launch("decode_attention_kernel");
 }

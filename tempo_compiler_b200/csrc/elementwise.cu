@@ -97,14 +97,14 @@ __global__ void block_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __re
 
 // ---- native LayerNorm: one warp per row, CPL 16-byte chunks per lane held in registers ----
 template <int CPL>
-__global__ void layernorm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ gamma,
-                                 const uint16_t* __restrict__ beta, uint16_t* __restrict__ out, uint32_t rows,
-                                 uint32_t features, float epsilon) {
+__global__ void layernorm_kernel(const uint16_t* __restrict__ x, uint32_t x_stride,
+                                 const uint16_t* __restrict__ gamma, const uint16_t* __restrict__ beta,
+                                 uint16_t* __restrict__ out, uint32_t rows, uint32_t features, float epsilon) {
   const uint32_t row = blockIdx.x * (blockDim.x / 32) + warp_id();
   if (row >= rows) return;
   const uint32_t lane = lane_id();
   const uint32_t chunks = features / 8;
-  const uint16_t* xr = x + size_t(row) * features;
+  const uint16_t* xr = x + size_t(row) * x_stride;
   float v[CPL][8];
   float sum = 0.f;
 #pragma unroll
@@ -187,7 +187,7 @@ __global__ void kv_store_kernel(const uint16_t* __restrict__ qkv, uint16_t* __re
 __global__ void argmax_finish_kernel(const float* __restrict__ part_val, const int32_t* __restrict__ part_idx,
                                      uint32_t rows, uint32_t tiles, int32_t* __restrict__ ids,
                                      int32_t* __restrict__ tokens_out, uint32_t out_stride,
-                                     int32_t* __restrict__ positions, int32_t advance) {
+                                     int32_t* __restrict__ positions, int32_t index_offset, int32_t advance) {
   const uint32_t row = blockIdx.x * (blockDim.x / 32) + warp_id();
   if (row >= rows) return;
   const uint32_t lane = lane_id();
@@ -206,7 +206,10 @@ __global__ void argmax_finish_kernel(const float* __restrict__ part_val, const i
   }
   if (lane == 0) {
     ids[row] = idx;
-    if (tokens_out != nullptr) tokens_out[size_t(row) * out_stride] = idx;
+    if (tokens_out != nullptr) {
+      const int32_t column = (positions != nullptr ? positions[row] : 0) + index_offset;
+      if (column >= 0 && uint32_t(column) < out_stride) tokens_out[size_t(row) * out_stride + column] = idx;
+    }
     if (positions != nullptr) positions[row] += advance;
   }
 }
@@ -250,10 +253,10 @@ extern "C" tempo_status tempo_block_copy(const void* source, void* destination, 
   return check_launch("block_copy_kernel");
 }
 
-extern "C" tempo_status tempo_layernorm(const void* x, const void* gamma, const void* beta, void* out, uint32_t rows,
-                                        uint32_t features, float epsilon, void* stream) {
-  if (rows == 0 || features == 0 || features % 8 || features > 4096)
-    return fail(TEMPO_ERR_VALUE, "tempo_layernorm: rows %u features %u", rows, features);
+extern "C" tempo_status tempo_layernorm(const void* x, uint32_t x_stride, const void* gamma, const void* beta,
+                                        void* out, uint32_t rows, uint32_t features, float epsilon, void* stream) {
+  if (rows == 0 || features == 0 || features % 8 || features > 4096 || x_stride < features || x_stride % 8)
+    return fail(TEMPO_ERR_VALUE, "tempo_layernorm: rows %u features %u stride %u", rows, features, x_stride);
   if (!aligned16(x) || !aligned16(gamma) || !aligned16(beta) || !aligned16(out))
     return fail(TEMPO_ERR_VALUE, "tempo_layernorm: operands must be 16-byte aligned");
   const uint32_t cpl = (features / 8 + 31) / 32;
@@ -263,12 +266,12 @@ extern "C" tempo_status tempo_layernorm(const void* x, const void* gamma, const 
   auto* gs = static_cast<const uint16_t*>(gamma);
   auto* bs = static_cast<const uint16_t*>(beta);
   auto* os = static_cast<uint16_t*>(out);
-  if (cpl <= 1) layernorm_kernel<1><<<grid, block, 0, st>>>(xs, gs, bs, os, rows, features, epsilon);
-  else if (cpl <= 2) layernorm_kernel<2><<<grid, block, 0, st>>>(xs, gs, bs, os, rows, features, epsilon);
-  else if (cpl <= 3) layernorm_kernel<3><<<grid, block, 0, st>>>(xs, gs, bs, os, rows, features, epsilon);
-  else if (cpl <= 4) layernorm_kernel<4><<<grid, block, 0, st>>>(xs, gs, bs, os, rows, features, epsilon);
-  else if (cpl <= 8) layernorm_kernel<8><<<grid, block, 0, st>>>(xs, gs, bs, os, rows, features, epsilon);
-  else layernorm_kernel<16><<<grid, block, 0, st>>>(xs, gs, bs, os, rows, features, epsilon);
+  if (cpl <= 1) layernorm_kernel<1><<<grid, block, 0, st>>>(xs, x_stride, gs, bs, os, rows, features, epsilon);
+  else if (cpl <= 2) layernorm_kernel<2><<<grid, block, 0, st>>>(xs, x_stride, gs, bs, os, rows, features, epsilon);
+  else if (cpl <= 3) layernorm_kernel<3><<<grid, block, 0, st>>>(xs, x_stride, gs, bs, os, rows, features, epsilon);
+  else if (cpl <= 4) layernorm_kernel<4><<<grid, block, 0, st>>>(xs, x_stride, gs, bs, os, rows, features, epsilon);
+  else if (cpl <= 8) layernorm_kernel<8><<<grid, block, 0, st>>>(xs, x_stride, gs, bs, os, rows, features, epsilon);
+  else layernorm_kernel<16><<<grid, block, 0, st>>>(xs, x_stride, gs, bs, os, rows, features, epsilon);
   return check_launch("layernorm_kernel");
 }
 
@@ -301,9 +304,10 @@ extern "C" tempo_status tempo_kv_store(const void* qkv, void* k_cache, void* v_c
 
 extern "C" tempo_status tempo_argmax_finish(const float* part_val, const int32_t* part_idx, uint32_t rows,
                                             uint32_t tiles, int32_t* ids, int32_t* tokens_out, uint32_t out_stride,
-                                            int32_t* positions, int32_t advance, void* stream) {
+                                            int32_t* positions, int32_t index_offset, int32_t advance,
+                                            void* stream) {
   if (rows == 0 || tiles == 0) return fail(TEMPO_ERR_VALUE, "tempo_argmax_finish: rows %u tiles %u", rows, tiles);
   argmax_finish_kernel<<<(rows + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      part_val, part_idx, rows, tiles, ids, tokens_out, out_stride, positions, advance);
+      part_val, part_idx, rows, tiles, ids, tokens_out, out_stride, positions, index_offset, advance);
   return check_launch("argmax_finish_kernel");
 }

@@ -1,0 +1,225 @@
+"""The B200-native GPT-2 engine: resident weights, batched prefill and greedy decode, one CUDA graph per decode step.
+
+The op order is the reference's layer (``_run_layer``, board_package/gpt2_inference.py:1133-1189) and the model chain
+its ``generate`` runs (:941-978): embed -> 12 x [LN1, QKV + bias, causal attention, proj + bias + residual, LN2,
+FC + bias + GELU, proj + bias + residual] -> final LN on the last token -> tied LM head -> greedy argmax. What changes
+is the B200 layout of the same math:
+
+* weights are uploaded once, transposed to [out, in] (K-major for the tensor cores), with the 1/sqrt(head) query
+  scale folded into the QKV weights and bias as the reference does (:1153-1168);
+* activations are row-major [tokens, features] for the whole batch, so each projection is one GEMM over every
+  token of every sequence (M = sequences x tokens) instead of one launch per 32-token block;
+* the bias, the exact-erf GELU (applied to the FC output, which the reference applies while staging the next GEMM's
+  input) and the residual add are fused into the GEMM epilogue, so the add images vanish;
+* keys and values are stored once per token into a [seq][head][position][64] cache, which decode attention streams;
+* the LM head's argmax is fused into its GEMM epilogue, so the 50257-wide logits never reach HBM;
+* the decode step (embedding, 12 layers, LM head, argmax, position advance) is captured once as a CUDA graph and
+  replayed, its varying state (ids, positions) living in device buffers.
+
+Every kernel is libtempo_b200.so's (through ``tempo_compiler_b200.ops``); torch only provides memory and streams.
+Sequences in one batch share one prompt length.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from tempo_compiler_b200 import ops
+from tempo_compiler_b200.weights import GPT2_SMALL, GPT2Shape
+
+LN_EPSILON = 1e-5
+
+
+def _bf16(array: np.ndarray, device) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(array, dtype=np.float32)).to(device).to(torch.bfloat16)
+
+
+@dataclass
+class LayerWeights:
+    ln1_g: torch.Tensor
+    ln1_b: torch.Tensor
+    w_qkv: torch.Tensor   # [3W, W], query rows scaled by 1/sqrt(head)
+    b_qkv: torch.Tensor
+    w_proj: torch.Tensor  # [W, W]
+    b_proj: torch.Tensor
+    ln2_g: torch.Tensor
+    ln2_b: torch.Tensor
+    w_fc: torch.Tensor    # [4W, W]
+    b_fc: torch.Tensor
+    w_out: torch.Tensor   # [W, 4W]
+    b_out: torch.Tensor
+
+
+class Engine:
+    """Batched GPT-2 greedy generation on one GPU.
+
+    Args:
+        layers, shared: weights as ``tempo_compiler_b200.weights.random_gpt2`` (or the reference's loader) returns them.
+        batch: sequences per batch.
+        prompt: tokens per prompt (every sequence of a batch has the same length).
+        capacity: cache positions per sequence (prompt + decode steps).
+        device: the CUDA device.
+    """
+
+    def __init__(self, layers: list[dict], shared: dict, *, batch: int, prompt: int, capacity: int,
+                 shape: GPT2Shape = GPT2_SMALL, device: str | torch.device = "cuda") -> None:
+        if not torch.cuda.is_available():
+            raise RuntimeError("the B200 engine needs a CUDA device; there is no CPU path")
+        self.device = torch.device(device)
+        self.shape = shape
+        self.batch, self.prompt, self.capacity = batch, prompt, capacity
+        if prompt > shape.positions or capacity > shape.positions + 1024:
+            raise ValueError(f"prompt {prompt} / capacity {capacity} exceed the model's {shape.positions} positions")
+        width, heads = shape.width, shape.heads
+        scale = np.ones(3 * width, dtype=np.float32)
+        scale[:width] = 1.0 / math.sqrt(width // heads)
+        self.layers: list[LayerWeights] = []
+        for w in layers:
+            self.layers.append(LayerWeights(
+                ln1_g=_bf16(w["ln_1.g"], self.device), ln1_b=_bf16(w["ln_1.b"], self.device),
+                w_qkv=_bf16((w["attn.qkv.w"] * scale).T, self.device), b_qkv=_bf16(w["attn.qkv.b"] * scale, self.device),
+                w_proj=_bf16(w["attn.proj.w"].T, self.device), b_proj=_bf16(w["attn.proj.b"], self.device),
+                ln2_g=_bf16(w["ln_2.g"], self.device), ln2_b=_bf16(w["ln_2.b"], self.device),
+                w_fc=_bf16(w["mlp.fc.w"].T, self.device), b_fc=_bf16(w["mlp.fc.b"], self.device),
+                w_out=_bf16(w["mlp.proj.w"].T, self.device), b_out=_bf16(w["mlp.proj.b"], self.device)))
+        self.wte = _bf16(shared["wte"], self.device)   # also the LM head's [vocab, W] operand
+        self.wpe = _bf16(shared["wpe"], self.device)
+        self.lnf_g = _bf16(shared["ln_f.g"], self.device)
+        self.lnf_b = _bf16(shared["ln_f.b"], self.device)
+        n_layers = len(layers)
+        cache_shape = (batch, heads, capacity, shape.head)
+        self.k_cache = [torch.empty(cache_shape, dtype=torch.bfloat16, device=self.device) for _ in range(n_layers)]
+        self.v_cache = [torch.empty(cache_shape, dtype=torch.bfloat16, device=self.device) for _ in range(n_layers)]
+        rows = batch * prompt
+        bf = dict(dtype=torch.bfloat16, device=self.device)
+        i32 = dict(dtype=torch.int32, device=self.device)
+        # prefill activations (all sequences at once)
+        self.x = torch.empty((rows, width), **bf)
+        self.ln = torch.empty((rows, width), **bf)
+        self.qkv = torch.empty((rows, 3 * width), **bf)
+        self.attn = torch.empty((rows, width), **bf)
+        self.h = torch.empty((rows, shape.ffn), **bf)
+        self.prompt_ids = torch.empty(rows, **i32)
+        self.prompt_pos = torch.arange(prompt, **i32).repeat(batch)
+        self.prompt_seq = torch.arange(batch, **i32).repeat_interleave(prompt)
+        # decode state
+        self.dx = torch.empty((batch, width), **bf)
+        self.dln = torch.empty((batch, width), **bf)
+        self.dqkv = torch.empty((batch, 3 * width), **bf)
+        self.dattn = torch.empty((batch, width), **bf)
+        self.dh = torch.empty((batch, shape.ffn), **bf)
+        self.ids = torch.zeros(batch, **i32)
+        self.positions = torch.zeros(batch, **i32)
+        self.seq_index = torch.arange(batch, **i32)
+        self.tiles = (shape.vocab + 255) // 256
+        self.part_val = torch.empty((batch, self.tiles), dtype=torch.float32, device=self.device)
+        self.part_idx = torch.empty((batch, self.tiles), **i32)
+        self.tokens: torch.Tensor | None = None
+        self._graph: torch.cuda.CUDAGraph | None = None
+        self._graph_steps = 0
+
+    # ---- prefill ---------------------------------------------------------------------------------------------
+
+    def _layer(self, lw: LayerWeights, index: int, x, ln, qkv, attn, h, *, decode: bool) -> None:
+        ops.layernorm(x, lw.ln1_g, lw.ln1_b, epsilon=LN_EPSILON, out=ln)
+        ops.gemm(ln, lw.w_qkv, bias=lw.b_qkv, out=qkv)
+        if decode:
+            ops.kv_store(qkv, self.k_cache[index], self.v_cache[index], self.seq_index, self.positions)
+            ops.decode_attention(qkv, self.k_cache[index], self.v_cache[index], self.positions, length_offset=1,
+                                 out=attn)
+        else:
+            ops.kv_store(qkv, self.k_cache[index], self.v_cache[index], self.prompt_seq, self.prompt_pos)
+            ops.attention_prefill(qkv, self.batch, self.prompt, self.shape.heads, out=attn)
+        ops.gemm(attn, lw.w_proj, bias=lw.b_proj, residual=x, out=x)
+        ops.layernorm(x, lw.ln2_g, lw.ln2_b, epsilon=LN_EPSILON, out=ln)
+        ops.gemm(ln, lw.w_fc, bias=lw.b_fc, gelu=True, out=h)
+        ops.gemm(h, lw.w_out, bias=lw.b_out, residual=x, out=x)
+
+    def prefill(self, token_ids: torch.Tensor) -> None:
+        """Runs the prompts ([batch, prompt] int32 on the device) through every layer, filling the caches, and writes
+        the first generated token of each sequence into ``self.tokens[:, 0]``."""
+        self.prompt_ids.copy_(token_ids.reshape(-1))
+        ops.embed(self.prompt_ids, self.prompt_pos, self.wte, self.wpe, out=self.x)
+        for index, lw in enumerate(self.layers):
+            self._layer(lw, index, self.x, self.ln, self.qkv, self.attn, self.h, decode=False)
+        # final LayerNorm on each sequence's last token only, then the LM head with its argmax fused
+        last = self.x[self.prompt - 1:]
+        ops.layernorm(last, self.lnf_g, self.lnf_b, epsilon=LN_EPSILON, out=self.dln, rows=self.batch,
+                      row_stride=self.prompt * self.shape.width)
+        self.positions.fill_(self.prompt)
+        self._head(index_offset=-self.prompt, advance=0)
+
+    def _head(self, *, index_offset: int, advance: int) -> None:
+        ops.gemm_argmax(self.dln, self.wte, self.part_val, self.part_idx)
+        ops.argmax_finish(self.part_val, self.part_idx, self.ids, tokens_out=self.tokens, positions=self.positions,
+                          index_offset=index_offset, advance=advance)
+
+    # ---- decode ----------------------------------------------------------------------------------------------
+
+    def _decode_step(self) -> None:
+        ops.embed(self.ids, self.positions, self.wte, self.wpe, out=self.dx)
+        for index, lw in enumerate(self.layers):
+            self._layer(lw, index, self.dx, self.dln, self.dqkv, self.dattn, self.dh, decode=True)
+        ops.layernorm(self.dx, self.lnf_g, self.lnf_b, epsilon=LN_EPSILON, out=self.dln)
+        # the token decoded at position p is generated token p - prompt + 1
+        self._head(index_offset=1 - self.prompt, advance=1)
+
+    def _capture(self) -> None:
+        if self._graph is not None:
+            return
+        saved_ids, saved_pos = self.ids.clone(), self.positions.clone()
+        saved_tokens = self.tokens.clone()
+        stream = torch.cuda.Stream(device=self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            self._decode_step()  # warm-up: kernel attributes and tensor-map encoders set up before capture
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self._decode_step()
+        self._graph = graph
+        # the warm-up and the capture advanced state: restore it
+        self.ids.copy_(saved_ids)
+        self.positions.copy_(saved_pos)
+        self.tokens.copy_(saved_tokens)
+
+    def decode(self, steps: int, *, graph: bool = True) -> None:
+        """Runs `steps` greedy decode steps, each consuming the last generated token."""
+        if steps <= 0:
+            return
+        if graph:
+            self._capture()
+            for _ in range(steps):
+                self._graph.replay()
+        else:
+            for _ in range(steps):
+                self._decode_step()
+
+    # ---- public API ------------------------------------------------------------------------------------------
+
+    def run(self, token_ids: torch.Tensor, steps: int, *, graph: bool = True) -> torch.Tensor:
+        """Prefill plus `steps` decode steps on device-resident prompts; returns [batch, steps + 1] int32 tokens."""
+        if token_ids.shape != (self.batch, self.prompt):
+            raise ValueError(f"expected prompts of shape {(self.batch, self.prompt)}, got {tuple(token_ids.shape)}")
+        if self.prompt + steps > self.capacity:
+            raise ValueError(f"{self.prompt} prompt tokens + {steps} steps exceed the cache capacity {self.capacity}")
+        if self.tokens is None or self.tokens.shape[1] != steps + 1:
+            self.tokens = torch.zeros((self.batch, steps + 1), dtype=torch.int32, device=self.device)
+            self._graph = None
+        self.prefill(token_ids)
+        self.decode(steps, graph=graph)
+        return self.tokens
+
+    def generate(self, token_ids: np.ndarray, steps: int, *, graph: bool = True) -> np.ndarray:
+        """The end-to-end call: host prompts in, host tokens out ([batch, steps + 1])."""
+        host = torch.from_numpy(np.ascontiguousarray(token_ids, dtype=np.int32)).pin_memory()
+        device_ids = host.to(self.device, non_blocking=True)
+        tokens = self.run(device_ids, steps, graph=graph)
+        out = torch.empty(tokens.shape, dtype=torch.int32, pin_memory=True)
+        out.copy_(tokens, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return out.numpy()

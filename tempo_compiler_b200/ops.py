@@ -12,8 +12,26 @@ import torch
 from tempo_compiler_b200 import lib as _lib
 
 
+_LAUNCHES = [0]
+
+
 def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
+
+
+def _launch(name: str, *args) -> None:
+    """Calls one kernel-launching entry point of the library (one kernel per call) and counts it."""
+    _LAUNCHES[0] += 1
+    _lib.call(name, *args)
+
+
+def reset_launch_count() -> None:
+    _LAUNCHES[0] = 0
+
+
+def launch_count() -> int:
+    """Kernel launches issued through this module since the last reset (graph replays are not counted)."""
+    return _LAUNCHES[0]
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -46,7 +64,7 @@ def gemm(a: torch.Tensor, w_t: torch.Tensor, *, bias: torch.Tensor | None = None
     if residual is not None:
         _check(residual, torch.bfloat16, "residual")
     flags = _lib.GEMM_GELU if gelu else 0
-    _lib.call("tempo_gemm", a.data_ptr(), k, w_t.data_ptr(), k, _ptr(bias), _ptr(residual), n, out.data_ptr(), n, m, n,
+    _launch("tempo_gemm", a.data_ptr(), k, w_t.data_ptr(), k, _ptr(bias), _ptr(residual), n, out.data_ptr(), n, m, n,
               k, flags, None, None, _stream())
     return out
 
@@ -57,26 +75,32 @@ def gemm_argmax(a: torch.Tensor, w_t: torch.Tensor, part_val: torch.Tensor, part
     _check(w_t, torch.bfloat16, "w_t")
     m, k = a.shape
     n = w_t.shape[0]
-    _lib.call("tempo_gemm", a.data_ptr(), k, w_t.data_ptr(), k, None, None, n, None, n, m, n, k, _lib.GEMM_ARGMAX,
+    _launch("tempo_gemm", a.data_ptr(), k, w_t.data_ptr(), k, None, None, n, None, n, m, n, k, _lib.GEMM_ARGMAX,
               part_val.data_ptr(), part_idx.data_ptr(), _stream())
 
 
 def argmax_finish(part_val: torch.Tensor, part_idx: torch.Tensor, ids: torch.Tensor, *,
-                  tokens_out: torch.Tensor | None = None, out_stride: int = 1, positions: torch.Tensor | None = None,
-                  advance: int = 0) -> None:
+                  tokens_out: torch.Tensor | None = None, positions: torch.Tensor | None = None,
+                  index_offset: int = 0, advance: int = 0) -> None:
+    """ids = per-row argmax; tokens_out[r, positions[r] + index_offset] = ids[r]; positions += advance."""
     rows, tiles = part_val.shape
-    _lib.call("tempo_argmax_finish", part_val.data_ptr(), part_idx.data_ptr(), rows, tiles, ids.data_ptr(),
-              _ptr(tokens_out), out_stride, _ptr(positions), advance, _stream())
+    stride = tokens_out.shape[1] if tokens_out is not None else 0
+    _launch("tempo_argmax_finish", part_val.data_ptr(), part_idx.data_ptr(), rows, tiles, ids.data_ptr(),
+              _ptr(tokens_out), stride, _ptr(positions), index_offset, advance, _stream())
 
 
 def layernorm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, *, epsilon: float = 1e-5,
-              out: torch.Tensor | None = None) -> torch.Tensor:
-    _check(x, torch.bfloat16, "x")
-    rows, features = x.shape
+              out: torch.Tensor | None = None, rows: int | None = None, row_stride: int | None = None) -> torch.Tensor:
+    """LayerNorm of `rows` rows of x read `row_stride` elements apart (default: every row of a contiguous x)."""
+    if not x.is_cuda or x.dtype != torch.bfloat16:
+        raise ValueError("x must be a CUDA bfloat16 tensor")
+    features = x.shape[-1]
+    rows = x.numel() // features if rows is None else rows
+    row_stride = features if row_stride is None else row_stride
     if out is None:
-        out = torch.empty_like(x)
-    _lib.call("tempo_layernorm", x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), out.data_ptr(), rows, features,
-              float(epsilon), _stream())
+        out = torch.empty((rows, features), dtype=torch.bfloat16, device=x.device)
+    _launch("tempo_layernorm", x.data_ptr(), row_stride, gamma.data_ptr(), beta.data_ptr(), out.data_ptr(), rows,
+              features, float(epsilon), _stream())
     return out
 
 
@@ -87,7 +111,7 @@ def embed(ids: torch.Tensor, positions: torch.Tensor, wte: torch.Tensor, wpe: to
     rows, width = ids.numel(), wte.shape[1]
     if out is None:
         out = torch.empty((rows, width), dtype=torch.bfloat16, device=wte.device)
-    _lib.call("tempo_embed", ids.data_ptr(), positions.data_ptr(), wte.data_ptr(), wpe.data_ptr(), out.data_ptr(), rows,
+    _launch("tempo_embed", ids.data_ptr(), positions.data_ptr(), wte.data_ptr(), wpe.data_ptr(), out.data_ptr(), rows,
               width, wte.shape[0], wpe.shape[0], _stream())
     return out
 
@@ -98,24 +122,24 @@ def attention_prefill(qkv: torch.Tensor, seqs: int, tokens: int, heads: int, *,
     width = qkv.shape[1] // 3
     if out is None:
         out = torch.empty((seqs * tokens, width), dtype=torch.bfloat16, device=qkv.device)
-    _lib.call("tempo_attention_prefill", qkv.data_ptr(), out.data_ptr(), seqs, tokens, heads, width // heads, _stream())
+    _launch("tempo_attention_prefill", qkv.data_ptr(), out.data_ptr(), seqs, tokens, heads, width // heads, _stream())
     return out
 
 
 def kv_store(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, seq_of: torch.Tensor,
              pos_of: torch.Tensor) -> None:
     seqs, heads, capacity, head = k_cache.shape
-    _lib.call("tempo_kv_store", qkv.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), seq_of.data_ptr(),
+    _launch("tempo_kv_store", qkv.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), seq_of.data_ptr(),
               pos_of.data_ptr(), seq_of.numel(), seqs, heads, head, capacity, _stream())
 
 
 def decode_attention(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, lengths: torch.Tensor, *,
-                     out: torch.Tensor | None = None) -> torch.Tensor:
+                     length_offset: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
     seqs, heads, capacity, head = k_cache.shape
     if out is None:
         out = torch.empty((seqs, heads * head), dtype=torch.bfloat16, device=qkv.device)
-    _lib.call("tempo_decode_attention", qkv.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), lengths.data_ptr(),
-              out.data_ptr(), seqs, heads, head, capacity, _stream())
+    _launch("tempo_decode_attention", qkv.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), lengths.data_ptr(),
+              length_offset, out.data_ptr(), seqs, heads, head, capacity, _stream())
     return out
 
 
@@ -123,30 +147,30 @@ def decode_attention(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
 
 def block_gemm(activations: torch.Tensor, weights: torch.Tensor, drain: torch.Tensor, bias: torch.Tensor | None,
                depth: int, columns: int, activate: bool) -> None:
-    _lib.call("tempo_block_gemm", activations.data_ptr(), weights.data_ptr(), drain.data_ptr(), _ptr(bias), depth,
+    _launch("tempo_block_gemm", activations.data_ptr(), weights.data_ptr(), drain.data_ptr(), _ptr(bias), depth,
               columns, int(activate), _stream())
 
 
 def block_add(left: torch.Tensor, right: torch.Tensor, out: torch.Tensor, features: int, broadcast: bool) -> None:
-    _lib.call("tempo_block_add", left.data_ptr(), right.data_ptr(), out.data_ptr(), features, int(broadcast), _stream())
+    _launch("tempo_block_add", left.data_ptr(), right.data_ptr(), out.data_ptr(), features, int(broadcast), _stream())
 
 
 def block_layernorm(rows: torch.Tensor, constants: torch.Tensor, out: torch.Tensor, features: int) -> None:
-    _lib.call("tempo_block_layernorm", rows.data_ptr(), constants.data_ptr(), out.data_ptr(), features, _stream())
+    _launch("tempo_block_layernorm", rows.data_ptr(), constants.data_ptr(), out.data_ptr(), features, _stream())
 
 
 def block_attention(constants: torch.Tensor, fused_operand: int, tokens: int, heads: int) -> None:
-    _lib.call("tempo_block_attention", constants.data_ptr(), fused_operand, tokens, heads, 64, _stream())
+    _launch("tempo_block_attention", constants.data_ptr(), fused_operand, tokens, heads, 64, _stream())
 
 
 def block_decode_attention(constants: torch.Tensor, cache_operand: int, fused_operand: int, keys: int, heads: int,
                            stated: int = 0) -> None:
-    _lib.call("tempo_block_decode_attention", constants.data_ptr(), cache_operand, fused_operand, keys, heads, 64,
+    _launch("tempo_block_decode_attention", constants.data_ptr(), cache_operand, fused_operand, keys, heads, 64,
               stated, _stream())
 
 
 def block_copy(source: int, destination: int, rows: int, stride: int) -> None:
-    _lib.call("tempo_block_copy", source, destination, rows, stride, _stream())
+    _launch("tempo_block_copy", source, destination, rows, stride, _stream())
 
 
 def watchdog() -> int:
