@@ -207,6 +207,18 @@ tempo_status tempo_argmax_finish(const float* part_val, const int32_t* part_idx,
                                  int32_t* ids, int32_t* tokens_out, uint32_t out_stride, int32_t* positions,
                                  int32_t index_offset, int32_t advance, void* stream);
 
+/* The LM head's greedy pick with no device allocation: ids[r] = the first j maximising hidden[r] . embedding[j], for
+ * hidden [rows, width] BF16 (row stride ld_hidden) and embedding [vocab, width] BF16 (row stride ld_embedding).
+ * No counterpart in the reference (its LM head runs on the host). It exists for callers that may not allocate device
+ * memory -- a plugin host that owns every device byte, or a loop that cannot pay for cudaMalloc/cudaFree -- and
+ * differs from tempo_gemm(TEMPO_GEMM_ARGMAX) + tempo_argmax_finish only in keeping their partials in a 2 MiB array
+ * inside the library, held on every GPU that loads it. Limits: 1 <= rows <= 1024 and 1 <= vocab <= 65536, else
+ * TEMPO_ERR_VALUE. The first call on a device looks up the array's address, so make it before any stream capture.
+ * Every call shares the array: calls whose work overlaps on the GPU race and must be ordered by the caller. */
+tempo_status tempo_lm_head_argmax_noalloc(const void* hidden, uint32_t ld_hidden, const void* embedding,
+                                          uint32_t ld_embedding, uint32_t rows, uint32_t vocab, uint32_t width,
+                                          int32_t* ids, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
