@@ -1,7 +1,7 @@
 // BF16 GEMMs on the 5th-generation tensor cores: TMA-fed, tcgen05.mma into TMEM accumulators, FP32 accumulate.
 //
-// Two kernels share the same warp-specialised pipeline (warp 0: TMA producer, warp 1: MMA issuer and TMEM owner,
-// warps 2-5: epilogue):
+// Two kernels share the same warp-specialised pipeline (warp 0: TMA producer, warp 1: MMA issuer and TMEM owner, the
+// rest epilogue: warps 2-9 in the row-major kernel, two per TMEM lane quarter; warps 2-5 in the block kernel):
 //
 //  * gemm_rowmajor_kernel -- the native engine's GEMM, out[M,N] = A[M,K] x W^T[N,K]^T, 128 x BN tiles, 64-deep
 //    stages in the 128-byte swizzled K-major layout, a persistent tile loop and a double-buffered accumulator so the
@@ -50,11 +50,18 @@ struct RowMajorSmem {
   static constexpr uint32_t kBarrierOffset = STAGES * kStageBytes;
   // full[S], empty[S], acc_full[2], acc_empty[2], final
   static constexpr uint32_t kBarriers = 2 * STAGES + 5;
-  static constexpr uint32_t kBytes = kBarrierOffset + kBarriers * 8 + 16 + 1024;  // + tmem slot, abort, alignment
+  static constexpr uint32_t kExchangeOffset = kBarrierOffset + kBarriers * 8 + 16;  // after tmem slot and abort flag
+  // argmax mode: the upper column half's best value and index per tile row, handed to the lower half
+  static constexpr uint32_t kBytes = kExchangeOffset + 128 * 8 + 1024;  // + alignment slack
 };
 
+// Warp roles of the row-major kernel: 0 TMA, 1 MMA, 2..9 epilogue. Epilogue warp w reads TMEM lane quarter w % 4
+// (the quarter a warp may access) and column half (w - 2) / 4 of each tile, so two warps share every row.
+constexpr int kRowThreads = 320;
+constexpr int kEpilogueThreads = 256;
+
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kRowThreads, 1)
     gemm_rowmajor_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                          RowMajorParams p) {
   using L = RowMajorSmem<BN, STAGES>;
@@ -82,7 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
+      mbar_init(&acc_empty[a], kEpilogueThreads);
     }
     mbar_init(final_bar, 1);
     *abort_flag = 0;
@@ -158,9 +165,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(final_bar, 0, kWatchOther, nullptr);
     }
   } else {
-    // Epilogue: warps 2..5 own TMEM lanes 32*(warp%4) .. +31, i.e. tile rows.
+    // Epilogue: warp owns TMEM lanes 32*(warp%4) .. +31 (tile rows) and one half of the tile's columns.
     const uint32_t lane_base = 32u * (warp & 3u);
     const uint32_t row_in_tile = lane_base + lane;
+    const uint32_t half = (warp - 2) >> 2;
+    constexpr uint32_t kHalf = BN / 2;
+    float* exchange_val = reinterpret_cast<float*>(smem + L::kExchangeOffset);
+    int32_t* exchange_idx = reinterpret_cast<int32_t*>(exchange_val + 128);
     uint32_t acc = 0, acc_phase = 0;
     const bool gelu = (p.flags & TEMPO_GEMM_GELU) != 0;
     const bool argmax = (p.flags & TEMPO_GEMM_ARGMAX) != 0;
@@ -173,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float best = -INFINITY;
       int32_t best_idx = 0;
 #pragma unroll 1
-      for (uint32_t c = 0; c < BN; c += 32) {
+      for (uint32_t c = half * kHalf; c < (half + 1) * kHalf; c += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + acc * BN + c, r);
         tmem_wait_ld();
@@ -249,9 +260,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (n0 + j < p.n) orow[n0 + j] = float_to_bf16(v[j]);
         }
       }
-      if (argmax && row_ok) {
-        p.part_val[size_t(row) * p.n_tiles + n_blk] = best;
-        p.part_idx[size_t(row) * p.n_tiles + n_blk] = best_idx;
+      if (argmax) {
+        // The upper half hands its best to the lower half, which keeps the earlier index on a tie.
+        const uint32_t pair_barrier = 1 + (warp & 3u);
+        if (half == 1) {
+          exchange_val[row_in_tile] = best;
+          exchange_idx[row_in_tile] = best_idx;
+        }
+        asm volatile("bar.sync %0, 64;" ::"r"(pair_barrier) : "memory");
+        if (half == 0 && row_ok) {
+          const float other = exchange_val[row_in_tile];
+          if (other > best) { best = other; best_idx = exchange_idx[row_in_tile]; }
+          p.part_val[size_t(row) * p.n_tiles + n_blk] = best;
+          p.part_idx[size_t(row) * p.n_tiles + n_blk] = best_idx;
+        }
+        asm volatile("bar.sync %0, 64;" ::"r"(pair_barrier) : "memory");
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
@@ -456,7 +479,7 @@ tempo_status launch_rowmajor(const void* a, uint32_t lda, const void* w_t, uint3
   auto kernel = gemm_rowmajor_kernel<BN, STAGES>;
   s = set_smem(reinterpret_cast<const void*>(kernel), L::kBytes);
   if (s != TEMPO_OK) return s;
-  kernel<<<grid, kThreads, L::kBytes, stream>>>(ta, tb, p);
+  kernel<<<grid, kRowThreads, L::kBytes, stream>>>(ta, tb, p);
   return check_launch("gemm_rowmajor_kernel");
 }
 

@@ -24,6 +24,7 @@ namespace tempo {
 
 int watchdog_gemm();
 int watchdog_attention();
+int watchdog_prefill();
 
 // ---------------------------------------------------------------------------------------------------------------
 // Errors and shared host helpers
@@ -153,13 +154,22 @@ void forget_images(uint64_t offset, uint64_t nbytes) {
   }
 }
 
+// Reads and clears every translation unit's watchdog; the first non-zero code, 0, or -1 if one could not be read.
+int read_watchdogs(int* gemm, int* decode, int* prefill) {
+  *gemm = watchdog_gemm();
+  *decode = watchdog_attention();
+  *prefill = watchdog_prefill();
+  if (*gemm < 0 || *decode < 0 || *prefill < 0) return -1;
+  return *gemm != 0 ? *gemm : (*decode != 0 ? *decode : *prefill);
+}
+
 tempo_status watchdog_status() {
-  const int a = watchdog_gemm();
-  const int b = watchdog_attention();
-  if (a < 0 || b < 0) return fail(TEMPO_ERR_RUNTIME, "could not read the device watchdog");
-  if (a != 0 || b != 0)
-    return fail(TEMPO_ERR_TIMEOUT, "a kernel gave up a bounded wait (watchdog codes gemm=%d attention=%d); its "
-                                   "results are not valid", a, b);
+  int a, b, c;
+  const int code = read_watchdogs(&a, &b, &c);
+  if (code < 0) return fail(TEMPO_ERR_RUNTIME, "could not read the device watchdog");
+  if (code != 0)
+    return fail(TEMPO_ERR_TIMEOUT, "a kernel gave up a bounded wait (watchdog codes gemm=%d decode=%d prefill=%d); "
+                                   "its results are not valid", a, b, c);
   return TEMPO_OK;
 }
 
@@ -386,9 +396,10 @@ extern "C" tempo_status tempo_stats(uint64_t* launches, uint64_t* arena_used) {
 }
 
 extern "C" tempo_status tempo_watchdog(int32_t* code) {
-  const int a = watchdog_gemm(), b = watchdog_attention();
-  *code = a != 0 ? a : b;
-  return (a < 0 || b < 0) ? fail(TEMPO_ERR_RUNTIME, "could not read the device watchdog") : TEMPO_OK;
+  int a, b, c;
+  const int value = read_watchdogs(&a, &b, &c);
+  *code = value < 0 ? 0 : value;
+  return value < 0 ? fail(TEMPO_ERR_RUNTIME, "could not read the device watchdog") : TEMPO_OK;
 }
 
 // ---------------------------------------------------------------------------------------------------------------
