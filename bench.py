@@ -199,23 +199,20 @@ def b200_arm(args) -> int:
         if world > 1:
             dist.barrier()
 
-    def max_over_ranks(value: float) -> float:
-        if world == 1:
-            return value
-        t = torch.tensor([value], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     from tempo_compiler_b200 import lib, ops
     from tempo_compiler_b200.engine import Engine
+    from tempo_compiler_b200.sharding import gather_tokens, shard
+    from tempo_compiler_b200.sharding import max_over_ranks as _max_over_ranks
     from tempo_compiler_b200.weights import random_gpt2, random_token_ids
+
+    def max_over_ranks(value: float) -> float:
+        return _max_over_ranks(value, device)
 
     lib.load()
     layers, shared = random_gpt2(args.seed)
-    per_rank = args.sequences // world
-    if per_rank * world != args.sequences:
-        raise SystemExit(f"{args.sequences} sequences do not shard evenly over {world} ranks")
-    first = rank * per_rank
+    first, per_rank = shard(args.sequences, world, rank)
+    if per_rank == 0:
+        raise SystemExit(f"{args.sequences} sequences leave rank {rank} of {world} without work")
     ids = np.stack([random_token_ids(args.seed + 1000 + s, args.prompt) for s in range(first, first + per_rank)])
     ids = ids.astype(np.int32)
     engine = Engine(layers, shared, batch=per_rank, prompt=args.prompt, capacity=args.prompt + args.decode,
@@ -270,7 +267,8 @@ def b200_arm(args) -> int:
     decode_ms = _time(lambda: engine.decode(args.decode, graph=graph), stream, 1) if args.decode else 0.0
     roof = _decode_attention_roofline(engine, stream, measured, source)
     gemm_roof = _gemm_roofline(engine, stream, measured, source)
-    watchdog = ops.watchdog()
+    watchdog = int(max_over_ranks(float(ops.watchdog())))
+    all_tokens = gather_tokens(torch.from_numpy(np.ascontiguousarray(tokens)), args.sequences, device)
 
     line = None
     if rank == 0:
@@ -284,7 +282,7 @@ def b200_arm(args) -> int:
                 "clocks": clock_info, "roofline": roof, "gemm_roofline": gemm_roof,
                 "phases_ms_rank0": {"prefill": prefill_ms, "decode": decode_ms},
                 "decode_graph": graph, "watchdog": watchdog,
-                "tokens_checksum": int(np.asarray(tokens, dtype=np.int64).sum())}
+                "tokens_checksum": int(all_tokens.to(torch.int64).sum().item())}
         if world == 1 and not args.no_cpu_baseline:
             seconds, count = cpu_sample(args, layers, shared)
             line["cpu_baseline"] = {

@@ -483,6 +483,281 @@ tempo_status launch_rowmajor(const void* a, uint32_t lda, const void* w_t, uint3
   return check_launch("gemm_rowmajor_kernel");
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Split-K for small M (the decode projections): a cluster of SPLITS CTAs shares one 128 x BN output tile, each CTA
+// running a contiguous share of the k-blocks into its own TMEM accumulator. The FP32 partial tiles are reduced
+// through distributed shared memory: CTA r owns rows [r*128/SPLITS, (r+1)*128/SPLITS) of the tile, every CTA writes
+// its partial rows into the owner's shared memory, one cluster barrier, and each owner sums its rows and runs the
+// epilogue with coalesced 16-byte stores. No workspace and no atomics.
+// ---------------------------------------------------------------------------------------------------------------
+
+template <int BN, int SPLITS, int STAGES>
+struct SplitSmem {
+  static constexpr uint32_t kABytes = 128 * kBK * 2;
+  static constexpr uint32_t kBBytes = BN * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kRowsPer = 128 / SPLITS;
+  static constexpr uint32_t kRedOffset = STAGES * kStageBytes;
+  static constexpr uint32_t kRedBytes = 128 * BN * 4;  // [SPLITS][kRowsPer][BN] FP32 partials of the owned rows
+  static constexpr uint32_t kBarrierOffset = kRedOffset + kRedBytes;
+  static constexpr uint32_t kBarriers = 2 * STAGES + 2;  // full, empty, acc_full, final
+  static constexpr uint32_t kBytes = kBarrierOffset + kBarriers * 8 + 16 + 1024;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t local_smem_addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_smem_addr), "r"(rank));
+  return remote;
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <int BN, int SPLITS, int STAGES>
+__global__ void __launch_bounds__(kRowThreads, 1)
+    gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                       RowMajorParams p) {
+  using L = SplitSmem<BN, SPLITS, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* red = reinterpret_cast<float*>(smem + L::kRedOffset);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarrierOffset);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* final_bar = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kBarriers);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_rank();
+  const uint32_t tile = blockIdx.x / SPLITS;
+  const uint32_t m_blk = tile / p.n_tiles, n_blk = tile % p.n_tiles;
+  const uint32_t kblocks = (p.k + kBK - 1) / kBK;
+  const uint32_t kb0 = rank * kblocks / SPLITS, kb1 = (rank + 1) * kblocks / SPLITS;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  bool have_acc = false;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      uint32_t stage = 0, phase = 0;
+      uint32_t last_parity[STAGES];
+      bool used[STAGES];
+      for (int s = 0; s < STAGES; ++s) used[s] = false;
+      for (uint32_t kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, kWatchEmpty, abort_flag)) break;
+        uint8_t* a_dst = smem + stage * L::kStageBytes;
+        mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+        tma_load_2d(a_dst, &tmap_a, &full[stage], int32_t(kb * kBK), int32_t(m_blk * 128));
+        tma_load_2d(a_dst + L::kABytes, &tmap_b, &full[stage], int32_t(kb * kBK), int32_t(n_blk * BN));
+        used[stage] = true;
+        last_parity[stage] = phase;
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      for (int s = 0; s < STAGES; ++s)
+        if (used[s]) mbar_wait(&full[s], last_parity[s], kWatchFull, nullptr);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc_bf16(128, BN, 0, 0);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (uint32_t kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full[stage], phase, kWatchFull, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+        const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+        for (uint32_t kk = 0; kk < kBK / 16; ++kk) {
+          const uint64_t a_desc = make_smem_desc(a_addr + kk * 32, 16, 1024, kLayoutSw128);
+          const uint64_t b_desc = make_smem_desc(b_addr + kk * 32, 16, 1024, kLayoutSw128);
+          umma_bf16(tmem_base, a_desc, b_desc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+        }
+        umma_commit(&empty[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+      if (ok) umma_commit(acc_full);
+      umma_commit(final_bar);
+      mbar_wait(final_bar, 0, kWatchOther, nullptr);
+    }
+  } else {
+    // Phase 1: this CTA's partial rows go to their owners' shared memory.
+    const uint32_t lane_base = 32u * (warp & 3u);
+    const uint32_t row_in_tile = lane_base + lane;
+    const uint32_t half = (warp - 2) >> 2;
+    constexpr uint32_t kHalf = BN / 2;
+    have_acc = mbar_wait(acc_full, 0, kWatchAccFull, abort_flag);
+    if (have_acc) {
+      tc_fence_after();
+      const uint32_t owner = row_in_tile / L::kRowsPer, owned_row = row_in_tile % L::kRowsPer;
+      const uint32_t local = smem_u32(red + (size_t(rank) * L::kRowsPer + owned_row) * BN);
+      const uint32_t remote = map_to_rank(local, owner);
+#pragma unroll 1
+      for (uint32_t c = half * kHalf; c < (half + 1) * kHalf; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 8; ++q) st_cluster_v4(remote + (c + q * 4) * 4, r[q * 4], r[q * 4 + 1], r[q * 4 + 2],
+                                                   r[q * 4 + 3]);
+      }
+    }
+  }
+  // Every partial has landed in its owner's shared memory.
+  cluster_sync_all();
+  if (warp >= 2 && !*abort_flag) {
+    // Phase 2: sum the owned rows' partials, then bias / GELU / residual and 16-byte BF16 stores.
+    const uint32_t t = threadIdx.x - 64;
+    constexpr uint32_t kChunks = BN / 8;
+    const bool gelu = (p.flags & TEMPO_GEMM_GELU) != 0;
+    for (uint32_t item = t; item < L::kRowsPer * kChunks; item += kEpilogueThreads) {
+      const uint32_t lr = item / kChunks, c8 = item % kChunks;
+      const uint32_t row = m_blk * 128 + rank * L::kRowsPer + lr;
+      const uint32_t col = n_blk * BN + c8 * 8;
+      if (row >= p.m || col >= p.n) continue;
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = 0.f;
+#pragma unroll
+      for (int s = 0; s < SPLITS; ++s) {
+        const float4* src = reinterpret_cast<const float4*>(red + (size_t(s) * L::kRowsPer + lr) * BN + c8 * 8);
+        const float4 x = src[0], y = src[1];
+        v[0] += x.x; v[1] += x.y; v[2] += x.z; v[3] += x.w;
+        v[4] += y.x; v[5] += y.y; v[6] += y.z; v[7] += y.w;
+      }
+      if (p.bias != nullptr) {
+        const uint4 w = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          v[2 * h] += bf16_lo(ws[h]);
+          v[2 * h + 1] += bf16_hi(ws[h]);
+        }
+      }
+      if (gelu) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = gelu_erf(round_bf16(v[j]));
+      }
+      if (p.residual != nullptr) {
+        const uint4 w = *reinterpret_cast<const uint4*>(p.residual + size_t(row) * p.ldr + col);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          v[2 * h] += bf16_lo(ws[h]);
+          v[2 * h + 1] += bf16_hi(ws[h]);
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16x2(v[0], v[1]);
+      o.y = pack_bf16x2(v[2], v[3]);
+      o.z = pack_bf16x2(v[4], v[5]);
+      o.w = pack_bf16x2(v[6], v[7]);
+      *reinterpret_cast<uint4*>(p.out + size_t(row) * p.ldo + col) = o;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+template <int BN, int SPLITS, int STAGES>
+tempo_status launch_splitk(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const RowMajorParams& base,
+                           cudaStream_t stream) {
+  using L = SplitSmem<BN, SPLITS, STAGES>;
+  CUtensorMap ta, tb;
+  const uint64_t a_dims[2] = {base.k, base.m};
+  const uint64_t a_strides[1] = {uint64_t(lda) * 2};
+  const uint32_t a_box[2] = {kBK, 128};
+  tempo_status s = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, a_dims, a_strides, a_box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != TEMPO_OK) return s;
+  const uint64_t b_dims[2] = {base.k, base.n};
+  const uint64_t b_strides[1] = {uint64_t(ldw) * 2};
+  const uint32_t b_box[2] = {kBK, uint32_t(BN)};
+  s = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_t, b_dims, b_strides, b_box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != TEMPO_OK) return s;
+  RowMajorParams p = base;
+  p.m_tiles = (p.m + 127) / 128;
+  p.n_tiles = (p.n + BN - 1) / BN;
+  auto kernel = gemm_splitk_kernel<BN, SPLITS, STAGES>;
+  s = set_smem(reinterpret_cast<const void*>(kernel), L::kBytes);
+  if (s != TEMPO_OK) return s;
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(p.m_tiles * p.n_tiles * SPLITS);
+  config.blockDim = dim3(kRowThreads);
+  config.dynamicSmemBytes = L::kBytes;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeClusterDimension;
+  attribute[0].val.clusterDim.x = SPLITS;
+  attribute[0].val.clusterDim.y = 1;
+  attribute[0].val.clusterDim.z = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&config, kernel, ta, tb, p);
+  if (err != cudaSuccess) return cuda_fail(err, "gemm_splitk_kernel launch");
+  return check_launch("gemm_splitk_kernel");
+}
+
+// Picks a split-K configuration for a GEMM whose 128-row tiles alone leave SMs idle: the most CTAs (tiles x splits)
+// that still fit one wave, each split keeping at least two k-blocks. Returns false when the plain kernel is better.
+bool pick_split(uint32_t m, uint32_t n, uint32_t k, uint32_t* bn, uint32_t* splits) {
+  const uint32_t sms = uint32_t(sm_count());
+  const uint32_t m_tiles = (m + 127) / 128, kblocks = (k + kBK - 1) / kBK;
+  if (uint64_t(m_tiles) * ((n + 127) / 128) >= sms) return false;
+  uint32_t best_ctas = 0;
+  for (uint32_t cand_bn : {128u, 64u}) {
+    const uint32_t tiles = m_tiles * ((n + cand_bn - 1) / cand_bn);
+    for (uint32_t s : {1u, 2u, 4u, 8u}) {
+      const uint64_t ctas = uint64_t(tiles) * s;
+      if (ctas > sms || kblocks < 2 * s) continue;
+      if (ctas > best_ctas) {
+        best_ctas = uint32_t(ctas);
+        *bn = cand_bn;
+        *splits = s;
+      }
+    }
+  }
+  return best_ctas > 0;
+}
+
 }  // namespace
 
 }  // namespace tempo
@@ -520,7 +795,25 @@ extern "C" tempo_status tempo_gemm(const void* a, uint32_t lda, const void* w_t,
   p.flags = flags;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (argmax) return launch_rowmajor<256, 4>(a, lda, w_t, ldw, p, st);
-  // Wide tiles when the grid still fills the GPU; narrower ones for the small-M decode GEMMs.
+  // Small M (decode): split the contraction over a cluster so every SM has work.
+  uint32_t bn = 0, splits = 0;
+  if (n % 8 == 0 && pick_split(m, n, k, &bn, &splits)) {
+    if (bn == 128) {
+      switch (splits) {
+        case 1: return launch_splitk<128, 1, 4>(a, lda, w_t, ldw, p, st);
+        case 2: return launch_splitk<128, 2, 4>(a, lda, w_t, ldw, p, st);
+        case 4: return launch_splitk<128, 4, 4>(a, lda, w_t, ldw, p, st);
+        default: return launch_splitk<128, 8, 4>(a, lda, w_t, ldw, p, st);
+      }
+    }
+    switch (splits) {
+      case 1: return launch_splitk<64, 1, 6>(a, lda, w_t, ldw, p, st);
+      case 2: return launch_splitk<64, 2, 6>(a, lda, w_t, ldw, p, st);
+      case 4: return launch_splitk<64, 4, 6>(a, lda, w_t, ldw, p, st);
+      default: return launch_splitk<64, 8, 6>(a, lda, w_t, ldw, p, st);
+    }
+  }
+  // Wide tiles when the grid still fills the GPU; narrower ones otherwise.
   const uint64_t tiles256 = uint64_t((m + 127) / 128) * ((n + 255) / 256);
   if (tiles256 >= uint64_t(sm_count())) return launch_rowmajor<256, 4>(a, lda, w_t, ldw, p, st);
   const uint64_t tiles128 = uint64_t((m + 127) / 128) * ((n + 127) / 128);

@@ -22,13 +22,20 @@ from tempo_compiler_b200 import lib, ops
 
 
 def _time(fn, repeats: int, warmup: int) -> float:
+    """Mean device time of one call: the `repeats` calls are captured into one CUDA graph and replayed, so host launch
+    cost (which exceeds the run time of the small decode kernels) does not enter the measurement."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(repeats):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
-    for _ in range(repeats):
-        fn()
+    graph.replay()
     end.record()
     torch.cuda.synchronize()
     return start.elapsed_time(end) / repeats

@@ -74,6 +74,46 @@ def random_gpt2(seed: int, shape: GPT2Shape = GPT2_SMALL, *, std: float = 0.02) 
     return layers, shared
 
 
+def save_gpt2_npz(path, layers: list[dict], shared: dict) -> None:
+    """Writes weights in the reference's export format: one BF16-word (uint16) array per tensor, per-layer names
+    prefixed ``h.<layer>.`` (tools/board/export_gpt2_weights.py:43-53)."""
+    arrays = {}
+    for index, layer in enumerate(layers):
+        for name, value in layer.items():
+            arrays[f"h.{index}.{name}"] = _words(value)
+    for name, value in shared.items():
+        arrays[name] = _words(value)
+    np.savez(path, **arrays)
+
+
+def load_gpt2_npz(path) -> tuple[list[dict], dict]:
+    """Reads the reference's exported weights (``gpt2_weights.npz``) as float32 arrays, split into per-layer dicts and
+    the shared dict the way the reference's loader splits them (board_package/gpt2_inference.py:315-342).
+
+    Raises:
+        FileNotFoundError: If the file does not exist.
+        ValueError: If a layer lacks one of the twelve tensors a GPT-2 block reads.
+    """
+    with np.load(path) as exported:
+        weights = {name: (exported[name].astype(np.uint32) << 16).view(np.float32) for name in exported.files}
+    layers: list[dict] = []
+    while f"h.{len(layers)}.ln_1.g" in weights:
+        prefix = f"h.{len(layers)}."
+        layer = {name[len(prefix):]: value for name, value in weights.items() if name.startswith(prefix)}
+        missing = [key for key in LAYER_KEYS if key not in layer]
+        if missing:
+            raise ValueError(f"layer {len(layers)} of {path} lacks {missing}")
+        layers.append(layer)
+    shared = {name: value for name, value in weights.items() if not name.startswith("h.")}
+    return layers, shared
+
+
+def _words(values: np.ndarray) -> np.ndarray:
+    """BF16 words (nearest even) of float32 values."""
+    return torch.from_numpy(np.ascontiguousarray(values, dtype=np.float32)).to(torch.bfloat16).view(torch.int16) \
+        .numpy().view(np.uint16)
+
+
 def random_token_ids(seed: int, count: int, vocab: int = GPT2_SMALL.vocab) -> np.ndarray:
     """Seeded token ids, uniform in [0, vocab)."""
     return np.random.default_rng(seed).integers(0, vocab, size=count, dtype=np.int64)

@@ -148,3 +148,19 @@ def test_reference_drivers_import_against_the_runtime_shim() -> None:
                 sys.modules.pop(name, None)
             else:
                 sys.modules[name] = value
+
+
+def test_weights_round_trip_through_the_reference_export_format(tmp_path) -> None:
+    """Weights saved in the reference's npz export format (BF16 words, ``h.<layer>.`` prefixes) load back exactly."""
+    from tempo_compiler_b200.weights import GPT2Shape, load_gpt2_npz, random_gpt2, save_gpt2_npz
+    layers, shared = random_gpt2(4, GPT2Shape(layers=2, vocab=300, positions=64))
+    path = tmp_path / "gpt2_weights.npz"
+    save_gpt2_npz(path, layers, shared)
+    loaded_layers, loaded_shared = load_gpt2_npz(path)
+    assert len(loaded_layers) == 2
+    for original, loaded in zip(layers, loaded_layers):
+        assert set(original) == set(loaded)
+        for name in original:
+            np.testing.assert_array_equal(original[name], loaded[name])
+    for name in shared:
+        np.testing.assert_array_equal(shared[name], loaded_shared[name])
