@@ -88,6 +88,8 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* _
                                                                const int32_t* __restrict__ lengths,
                                                                int32_t length_offset, uint16_t* __restrict__ out,
                                                                uint32_t heads, uint32_t capacity) {
+  pdl_launch_dependents();
+  pdl_wait();
   const uint32_t h = blockIdx.x, s = blockIdx.y;
   const uint32_t warp = warp_id(), lane = lane_id();
   const uint32_t g = lane >> 3, li = lane & 7u;
@@ -233,8 +235,8 @@ extern "C" tempo_status tempo_decode_attention(const void* qkv, const void* k_ca
                 capacity);
   if (!aligned16(qkv) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
     return fail(TEMPO_ERR_VALUE, "tempo_decode_attention: operands must be 16-byte aligned");
-  decode_attention_kernel<<<dim3(heads, seqs), 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t*>(qkv), static_cast<const uint16_t*>(k_cache), static_cast<const uint16_t*>(v_cache),
-      lengths, length_offset, static_cast<uint16_t*>(out), heads, capacity);
-  return check_launch("decode_attention_kernel");
+  return launch(decode_attention_kernel, dim3(heads, seqs), dim3(128), 0, static_cast<cudaStream_t>(stream), 1,
+                "decode_attention_kernel", static_cast<const uint16_t*>(qkv), static_cast<const uint16_t*>(k_cache),
+                static_cast<const uint16_t*>(v_cache), lengths, length_offset, static_cast<uint16_t*>(out), heads,
+                capacity);
 }

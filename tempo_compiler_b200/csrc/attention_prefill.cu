@@ -122,6 +122,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t tmem_s = tmem_base;        // 128 columns: S (FP32), then P (BF16 pairs) in its first 64
   const uint32_t tmem_o = tmem_base + 128;  // 64 columns: O (FP32)
+  pdl_launch_dependents();
+  pdl_wait();  // Q, K and V are the previous kernel's output
 
   auto tile_coord = [&](uint32_t t) -> int32_t {
     if constexpr (PACKED) return int32_t(t * 4);
@@ -335,8 +337,8 @@ extern "C" tempo_status tempo_block_attention(const void* constants, void* fused
   p.q_tiles = (tokens + 127) / 128;
   p.block_bytes = block_bytes;
   if ((s = set_smem(reinterpret_cast<const void*>(attention_prefill_kernel<true>), kSmem))) return s;
-  attention_prefill_kernel<true><<<p.q_tiles * heads, kThreads, kSmem, static_cast<cudaStream_t>(stream)>>>(map, p);
-  return check_launch("attention_prefill_kernel<packed>");
+  return launch(attention_prefill_kernel<true>, dim3(p.q_tiles * heads), dim3(kThreads), kSmem,
+                static_cast<cudaStream_t>(stream), 1, "attention_prefill_kernel<packed>", map, p);
 }
 
 extern "C" tempo_status tempo_attention_prefill(const void* qkv, void* out, uint32_t seqs, uint32_t tokens,
@@ -362,6 +364,6 @@ extern "C" tempo_status tempo_attention_prefill(const void* qkv, void* out, uint
   const uint64_t ctas = uint64_t(p.q_tiles) * heads * seqs;
   if (ctas > 0x7FFFFFFFull) return fail(TEMPO_ERR_VALUE, "tempo_attention_prefill: too many tiles");
   if ((s = set_smem(reinterpret_cast<const void*>(attention_prefill_kernel<false>), kSmem))) return s;
-  attention_prefill_kernel<false><<<uint32_t(ctas), kThreads, kSmem, static_cast<cudaStream_t>(stream)>>>(map, p);
-  return check_launch("attention_prefill_kernel<rowmajor>");
+  return launch(attention_prefill_kernel<false>, dim3(uint32_t(ctas)), dim3(kThreads), kSmem,
+                static_cast<cudaStream_t>(stream), 1, "attention_prefill_kernel<rowmajor>", map, p);
 }

@@ -281,6 +281,20 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(uint32_t m, uint32_t n, u
          | ((m >> 4) << 24);  // M / 16
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may start while the
+// kernel before it in the stream is still running. It does its independent set-up (barriers, TMEM, weight
+// prefetch), then waits for that kernel's completion and memory before touching anything the kernel wrote.
+// Without the launch attribute both instructions are no-ops.
+// ---------------------------------------------------------------------------------------------------------------
+
+// Blocks until every prerequisite grid has completed and its memory operations are visible.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the next grid in the stream begin launching once every CTA of this grid has executed it (or exited). Called
+// after this CTA holds its tensor memory, so a dependent CTA can never take TMEM this grid still needs.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 __device__ __forceinline__ uint32_t warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
 

@@ -100,6 +100,8 @@ template <int CPL>
 __global__ void layernorm_kernel(const uint16_t* __restrict__ x, uint32_t x_stride,
                                  const uint16_t* __restrict__ gamma, const uint16_t* __restrict__ beta,
                                  uint16_t* __restrict__ out, uint32_t rows, uint32_t features, float epsilon) {
+  pdl_launch_dependents();
+  pdl_wait();
   const uint32_t row = blockIdx.x * (blockDim.x / 32) + warp_id();
   if (row >= rows) return;
   const uint32_t lane = lane_id();
@@ -147,6 +149,8 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const int32_t* __r
                              const uint16_t* __restrict__ wte, const uint16_t* __restrict__ wpe,
                              uint16_t* __restrict__ x, uint32_t rows, uint32_t width, uint32_t vocab,
                              uint32_t max_positions) {
+  pdl_launch_dependents();
+  pdl_wait();
   const uint32_t per_row = width / 8;
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * per_row) return;
@@ -168,6 +172,8 @@ __global__ void kv_store_kernel(const uint16_t* __restrict__ qkv, uint16_t* __re
                                 uint16_t* __restrict__ v_cache, const int32_t* __restrict__ seq_of,
                                 const int32_t* __restrict__ pos_of, uint32_t rows, uint32_t seqs, uint32_t heads,
                                 uint32_t head, uint32_t capacity) {
+  pdl_launch_dependents();
+  pdl_wait();
   const uint32_t width = heads * head;
   const uint32_t per_row = 2 * width / 8;  // 16-byte vectors of keys then values
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -188,6 +194,8 @@ __global__ void argmax_finish_kernel(const float* __restrict__ part_val, const i
                                      uint32_t rows, uint32_t tiles, int32_t* __restrict__ ids,
                                      int32_t* __restrict__ tokens_out, uint32_t out_stride,
                                      int32_t* __restrict__ positions, int32_t index_offset, int32_t advance) {
+  pdl_launch_dependents();
+  pdl_wait();
   const uint32_t row = blockIdx.x * (blockDim.x / 32) + warp_id();
   if (row >= rows) return;
   const uint32_t lane = lane_id();
@@ -266,13 +274,13 @@ extern "C" tempo_status tempo_layernorm(const void* x, uint32_t x_stride, const 
   auto* gs = static_cast<const uint16_t*>(gamma);
   auto* bs = static_cast<const uint16_t*>(beta);
   auto* os = static_cast<uint16_t*>(out);
-  if (cpl <= 1) layernorm_kernel<1><<<grid, block, 0, st>>>(xs, x_stride, gs, bs, os, rows, features, epsilon);
-  else if (cpl <= 2) layernorm_kernel<2><<<grid, block, 0, st>>>(xs, x_stride, gs, bs, os, rows, features, epsilon);
-  else if (cpl <= 3) layernorm_kernel<3><<<grid, block, 0, st>>>(xs, x_stride, gs, bs, os, rows, features, epsilon);
-  else if (cpl <= 4) layernorm_kernel<4><<<grid, block, 0, st>>>(xs, x_stride, gs, bs, os, rows, features, epsilon);
-  else if (cpl <= 8) layernorm_kernel<8><<<grid, block, 0, st>>>(xs, x_stride, gs, bs, os, rows, features, epsilon);
-  else layernorm_kernel<16><<<grid, block, 0, st>>>(xs, x_stride, gs, bs, os, rows, features, epsilon);
-  return check_launch("layernorm_kernel");
+  auto kernel = cpl <= 1 ? layernorm_kernel<1>
+              : cpl <= 2 ? layernorm_kernel<2>
+              : cpl <= 3 ? layernorm_kernel<3>
+              : cpl <= 4 ? layernorm_kernel<4>
+              : cpl <= 8 ? layernorm_kernel<8>
+                         : layernorm_kernel<16>;
+  return launch(kernel, grid, block, 0, st, 1, "layernorm_kernel", xs, x_stride, gs, bs, os, rows, features, epsilon);
 }
 
 extern "C" tempo_status tempo_embed(const int32_t* ids, const int32_t* positions, const void* wte, const void* wpe,
@@ -282,10 +290,9 @@ extern "C" tempo_status tempo_embed(const int32_t* ids, const int32_t* positions
   if (!aligned16(wte) || !aligned16(wpe) || !aligned16(x))
     return fail(TEMPO_ERR_VALUE, "tempo_embed: operands must be 16-byte aligned");
   const uint64_t threads = uint64_t(rows) * (width / 8);
-  embed_kernel<<<uint32_t((threads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      ids, positions, static_cast<const uint16_t*>(wte), static_cast<const uint16_t*>(wpe), static_cast<uint16_t*>(x),
-      rows, width, vocab, max_positions);
-  return check_launch("embed_kernel");
+  return launch(embed_kernel, dim3(uint32_t((threads + 255) / 256)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                1, "embed_kernel", ids, positions, static_cast<const uint16_t*>(wte),
+                static_cast<const uint16_t*>(wpe), static_cast<uint16_t*>(x), rows, width, vocab, max_positions);
 }
 
 extern "C" tempo_status tempo_kv_store(const void* qkv, void* k_cache, void* v_cache, const int32_t* seq_of,
@@ -296,10 +303,9 @@ extern "C" tempo_status tempo_kv_store(const void* qkv, void* k_cache, void* v_c
   if (!aligned16(qkv) || !aligned16(k_cache) || !aligned16(v_cache))
     return fail(TEMPO_ERR_VALUE, "tempo_kv_store: operands must be 16-byte aligned");
   const uint64_t threads = uint64_t(rows) * (2 * heads * head / 8);
-  kv_store_kernel<<<uint32_t((threads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t*>(qkv), static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), seq_of,
-      pos_of, rows, seqs, heads, head, capacity);
-  return check_launch("kv_store_kernel");
+  return launch(kv_store_kernel, dim3(uint32_t((threads + 255) / 256)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                1, "kv_store_kernel", static_cast<const uint16_t*>(qkv), static_cast<uint16_t*>(k_cache),
+                static_cast<uint16_t*>(v_cache), seq_of, pos_of, rows, seqs, heads, head, capacity);
 }
 
 extern "C" tempo_status tempo_argmax_finish(const float* part_val, const int32_t* part_idx, uint32_t rows,
@@ -307,7 +313,7 @@ extern "C" tempo_status tempo_argmax_finish(const float* part_val, const int32_t
                                             int32_t* positions, int32_t index_offset, int32_t advance,
                                             void* stream) {
   if (rows == 0 || tiles == 0) return fail(TEMPO_ERR_VALUE, "tempo_argmax_finish: rows %u tiles %u", rows, tiles);
-  argmax_finish_kernel<<<(rows + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      part_val, part_idx, rows, tiles, ids, tokens_out, out_stride, positions, index_offset, advance);
-  return check_launch("argmax_finish_kernel");
+  return launch(argmax_finish_kernel, dim3((rows + 7) / 8), dim3(256), 0, static_cast<cudaStream_t>(stream), 1,
+                "argmax_finish_kernel", part_val, part_idx, rows, tiles, ids, tokens_out, out_stride, positions,
+                index_offset, advance);
 }

@@ -105,6 +105,9 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  // Everything below reads operands or writes outputs the previous kernel in the stream may still be using.
+  pdl_wait();
 
   if (warp == 0) {
     if (elect_one()) {
@@ -479,8 +482,7 @@ tempo_status launch_rowmajor(const void* a, uint32_t lda, const void* w_t, uint3
   auto kernel = gemm_rowmajor_kernel<BN, STAGES>;
   s = set_smem(reinterpret_cast<const void*>(kernel), L::kBytes);
   if (s != TEMPO_OK) return s;
-  kernel<<<grid, kRowThreads, L::kBytes, stream>>>(ta, tb, p);
-  return check_launch("gemm_rowmajor_kernel");
+  return launch(kernel, dim3(grid), dim3(kRowThreads), L::kBytes, stream, 1, "gemm_rowmajor_kernel", ta, tb, p);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -569,6 +571,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
   bool have_acc = false;
 
   if (warp == 0) {
@@ -577,12 +580,24 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       uint32_t last_parity[STAGES];
       bool used[STAGES];
       for (int s = 0; s < STAGES; ++s) used[s] = false;
+      // The weights do not depend on the previous kernel: the first ring's worth streams in before the wait.
+      const uint32_t early = (kb1 - kb0) < uint32_t(STAGES) ? (kb1 - kb0) : uint32_t(STAGES);
+      for (uint32_t i = 0; i < early; ++i) {
+        mbar_arrive_expect_tx(&full[i], L::kStageBytes);
+        tma_load_2d(smem + i * L::kStageBytes + L::kABytes, &tmap_b, &full[i], int32_t((kb0 + i) * kBK),
+                    int32_t(n_blk * BN));
+        used[i] = true;  // a copy is in flight on this stage from here on
+        last_parity[i] = 0;
+      }
+      pdl_wait();
       for (uint32_t kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, kWatchEmpty, abort_flag)) break;
         uint8_t* a_dst = smem + stage * L::kStageBytes;
-        mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+        if (kb - kb0 >= early) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, kWatchEmpty, abort_flag)) break;
+          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          tma_load_2d(a_dst + L::kABytes, &tmap_b, &full[stage], int32_t(kb * kBK), int32_t(n_blk * BN));
+        }
         tma_load_2d(a_dst, &tmap_a, &full[stage], int32_t(kb * kBK), int32_t(m_blk * 128));
-        tma_load_2d(a_dst + L::kABytes, &tmap_b, &full[stage], int32_t(kb * kBK), int32_t(n_blk * BN));
         used[stage] = true;
         last_parity[stage] = phase;
         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -639,7 +654,9 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   // Every partial has landed in its owner's shared memory.
   cluster_sync_all();
   if (warp >= 2 && !*abort_flag) {
-    // Phase 2: sum the owned rows' partials, then bias / GELU / residual and 16-byte BF16 stores.
+    // Phase 2: sum the owned rows' partials, then bias / GELU / residual and 16-byte BF16 stores. The residual and
+    // the output may be the previous kernel's operands: wait for it (already finished, as the A operand was).
+    pdl_wait();
     const uint32_t t = threadIdx.x - 64;
     constexpr uint32_t kChunks = BN / 8;
     const bool gelu = (p.flags & TEMPO_GEMM_GELU) != 0;
@@ -719,21 +736,8 @@ tempo_status launch_splitk(const void* a, uint32_t lda, const void* w_t, uint32_
   auto kernel = gemm_splitk_kernel<BN, SPLITS, STAGES>;
   s = set_smem(reinterpret_cast<const void*>(kernel), L::kBytes);
   if (s != TEMPO_OK) return s;
-  cudaLaunchConfig_t config = {};
-  config.gridDim = dim3(p.m_tiles * p.n_tiles * SPLITS);
-  config.blockDim = dim3(kRowThreads);
-  config.dynamicSmemBytes = L::kBytes;
-  config.stream = stream;
-  cudaLaunchAttribute attribute[1];
-  attribute[0].id = cudaLaunchAttributeClusterDimension;
-  attribute[0].val.clusterDim.x = SPLITS;
-  attribute[0].val.clusterDim.y = 1;
-  attribute[0].val.clusterDim.z = 1;
-  config.attrs = attribute;
-  config.numAttrs = 1;
-  const cudaError_t err = cudaLaunchKernelEx(&config, kernel, ta, tb, p);
-  if (err != cudaSuccess) return cuda_fail(err, "gemm_splitk_kernel launch");
-  return check_launch("gemm_splitk_kernel");
+  return launch(kernel, dim3(p.m_tiles * p.n_tiles * SPLITS), dim3(kRowThreads), L::kBytes, stream, SPLITS,
+                "gemm_splitk_kernel", ta, tb, p);
 }
 
 // Picks a split-K configuration for a GEMM whose 128-row tiles alone leave SMs idle: the most CTAs (tiles x splits)

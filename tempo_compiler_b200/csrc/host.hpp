@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/tempo_b200.h"
 
@@ -36,5 +37,35 @@ int sm_count();
 tempo_status set_smem(const void* kernel, int bytes);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launches `kernel` with programmatic stream serialization (it may overlap the tail of the previous kernel in the
+// stream; the kernel itself waits with griddepcontrol.wait before reading anything that kernel wrote) and, when
+// cluster_x > 1, as clusters of cluster_x CTAs along x.
+template <typename... KernelArgs, typename... Args>
+tempo_status launch(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                    unsigned cluster_x, const char* name, Args&&... args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attributes[2];
+  unsigned count = 0;
+  attributes[count].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attributes[count].val.programmaticStreamSerializationAllowed = 1;
+  ++count;
+  if (cluster_x > 1) {
+    attributes[count].id = cudaLaunchAttributeClusterDimension;
+    attributes[count].val.clusterDim.x = cluster_x;
+    attributes[count].val.clusterDim.y = 1;
+    attributes[count].val.clusterDim.z = 1;
+    ++count;
+  }
+  config.attrs = attributes;
+  config.numAttrs = count;
+  const cudaError_t err = cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
+  if (err != cudaSuccess) return cuda_fail(err, name);
+  return check_launch(name);
+}
 
 }  // namespace tempo
