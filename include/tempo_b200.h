@@ -171,6 +171,17 @@ tempo_status tempo_gemm(const void* a, uint32_t lda, const void* w_t, uint32_t l
                         const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m, uint32_t n,
                         uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx, void* stream);
 
+/* The QKV projection with the KV-cache write fused into its epilogue: out[M, 3*heads*head] = a x w_t^T + bias as
+ * tempo_gemm computes it, and each row's key and value columns are also stored into k_cache / v_cache
+ * ([seqs][heads][capacity][head] BF16) -- row r being sequence r / tokens_per_seq at position r % tokens_per_seq
+ * (prefill), or, when positions is not NULL, sequence r at positions[r] (decode). Rows whose sequence or position is
+ * out of range are not stored. Replaces the copy images that fill the reference's KV cache
+ * (KVCache.extend/append, board_package/gpt2_inference.py:253-293). head % 32 == 0. */
+tempo_status tempo_gemm_qkv(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias, void* out,
+                            uint32_t ldo, uint32_t m, uint32_t k, void* k_cache, void* v_cache, uint32_t seqs,
+                            uint32_t heads, uint32_t head, uint32_t capacity, uint32_t tokens_per_seq,
+                            const int32_t* positions, void* stream);
+
 /* Row-wise LayerNorm of `rows` BF16 rows of `features` (features % 8 == 0, <= 4096) read `x_stride` elements apart
  * (x_stride % 8 == 0), FP32 statistics, BF16 out [rows, features]. */
 tempo_status tempo_layernorm(const void* x, uint32_t x_stride, const void* gamma, const void* beta, void* out,

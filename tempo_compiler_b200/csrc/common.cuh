@@ -295,6 +295,32 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 // after this CTA holds its tensor memory, so a dependent CTA can never take TMEM this grid still needs.
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
+// ---------------------------------------------------------------------------------------------------------------
+// KV-cache store fused into the QKV projection's epilogue
+// ---------------------------------------------------------------------------------------------------------------
+
+// Where the QKV product's key and value columns also go: caches [seqs][heads][capacity][head]. Row r of the product
+// is sequence r / tokens at position r % tokens (prefill), or sequence r at positions[r] (decode).
+struct KvStore {
+  uint16_t* k;  // null: no cache store
+  uint16_t* v;
+  const int32_t* positions;
+  uint32_t tokens, seqs, heads, head, capacity, width;  // width = heads * head (the query columns)
+};
+
+// The cache address of columns [col, col + count) of row `row` when they are key or value columns (count stays
+// inside one head), or null.
+__device__ __forceinline__ uint16_t* kv_destination(const KvStore& kv, uint32_t row, uint32_t col) {
+  if (kv.k == nullptr || col < kv.width) return nullptr;
+  const uint32_t which = (col - kv.width) / kv.width;
+  const uint32_t feature = (col - kv.width) % kv.width;
+  const uint32_t seq = kv.positions != nullptr ? row : row / kv.tokens;
+  const uint32_t pos = kv.positions != nullptr ? uint32_t(kv.positions[row]) : row % kv.tokens;
+  if (which > 1 || seq >= kv.seqs || pos >= kv.capacity) return nullptr;
+  return (which ? kv.v : kv.k) + ((size_t(seq) * kv.heads + feature / kv.head) * kv.capacity + pos) * kv.head +
+         feature % kv.head;
+}
+
 __device__ __forceinline__ uint32_t warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
 

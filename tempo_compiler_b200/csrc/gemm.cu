@@ -25,6 +25,12 @@ namespace tempo {
 
 TEMPO_WATCHDOG_READER(watchdog_gemm)
 
+// gemv.cu: the bandwidth-bound path for at most 8 rows (TEMPO_ERR_VALUE when it does not apply).
+tempo_status gemv_dispatch(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
+                           const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m, uint32_t n,
+                           uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx, const KvStore& kv,
+                           cudaStream_t stream);
+
 namespace {
 
 constexpr int kThreads = 192;  // 6 warps
@@ -40,6 +46,7 @@ struct RowMajorParams {
   uint32_t ldo, ldr;
   uint32_t flags;
   uint32_t m_tiles, n_tiles;
+  KvStore kv;  // QKV projection: key and value columns also stored into the caches
 };
 
 template <int BN, int STAGES>
@@ -249,6 +256,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
         }
         if (full_chunk) {
           uint4* o4 = reinterpret_cast<uint4*>(orow + n0);
+          uint4* cache4 = reinterpret_cast<uint4*>(kv_destination(p.kv, row, n0));
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint4 w;
@@ -257,6 +265,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
             w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
             w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
             o4[q] = w;
+            if (cache4 != nullptr) cache4[q] = w;
           }
         } else {
           for (int j = 0; j < 32; ++j)
@@ -703,6 +712,8 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       o.z = pack_bf16x2(v[4], v[5]);
       o.w = pack_bf16x2(v[6], v[7]);
       *reinterpret_cast<uint4*>(p.out + size_t(row) * p.ldo + col) = o;
+      uint4* cache4 = reinterpret_cast<uint4*>(kv_destination(p.kv, row, col));
+      if (cache4 != nullptr) *cache4 = o;
     }
   }
 
@@ -768,10 +779,39 @@ bool pick_split(uint32_t m, uint32_t n, uint32_t k, uint32_t* bn, uint32_t* spli
 
 using namespace tempo;
 
+static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
+                              const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m, uint32_t n,
+                              uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx, const KvStore& kv,
+                              void* stream);
+
 extern "C" tempo_status tempo_gemm(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
                                    const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m,
                                    uint32_t n, uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx,
                                    void* stream) {
+  return gemm_impl(a, lda, w_t, ldw, bias, residual, ldr, out, ldo, m, n, k, flags, part_val, part_idx, KvStore{},
+                   stream);
+}
+
+extern "C" tempo_status tempo_gemm_qkv(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
+                                       void* out, uint32_t ldo, uint32_t m, uint32_t k, void* k_cache, void* v_cache,
+                                       uint32_t seqs, uint32_t heads, uint32_t head, uint32_t capacity,
+                                       uint32_t tokens_per_seq, const int32_t* positions, void* stream) {
+  const uint32_t width = heads * head;
+  if (k_cache == nullptr || v_cache == nullptr || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm_qkv: both caches are needed, 16-byte aligned");
+  if (heads == 0 || head == 0 || head % 32 || seqs == 0 || capacity == 0 ||
+      (positions == nullptr && tokens_per_seq == 0))
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm_qkv: heads %u head %u (multiple of 32) seqs %u capacity %u tokens %u",
+                heads, head, seqs, capacity, tokens_per_seq);
+  KvStore kv{static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), positions, tokens_per_seq, seqs,
+             heads, head, capacity, width};
+  return gemm_impl(a, lda, w_t, ldw, bias, nullptr, 0, out, ldo, m, 3 * width, k, 0, nullptr, nullptr, kv, stream);
+}
+
+static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
+                              const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m, uint32_t n,
+                              uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx, const KvStore& kv,
+                              void* stream) {
   if (m == 0 || n == 0 || k == 0) return fail(TEMPO_ERR_VALUE, "tempo_gemm: empty problem %ux%ux%u", m, n, k);
   if (k % 8 || lda % 8 || ldw % 8 || lda < k || ldw < k)
     return fail(TEMPO_ERR_VALUE, "tempo_gemm: K (%u) and the row strides (%u, %u) must be multiples of 8 and >= K", k,
@@ -797,7 +837,14 @@ extern "C" tempo_status tempo_gemm(const void* a, uint32_t lda, const void* w_t,
   p.ldo = ldo;
   p.ldr = ldr;
   p.flags = flags;
+  p.kv = kv;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // A handful of rows (decode of a few sequences): stream the weights on the CUDA cores instead.
+  if (m <= 8) {
+    const tempo_status gemv = gemv_dispatch(a, lda, w_t, ldw, bias, residual, ldr, out, ldo, m, n, k, flags, part_val,
+                                            part_idx, kv, st);
+    if (gemv != TEMPO_ERR_VALUE) return gemv;
+  }
   if (argmax) return launch_rowmajor<256, 4>(a, lda, w_t, ldw, p, st);
   // Small M (decode): split the contraction over a cluster so every SM has work.
   uint32_t bn = 0, splits = 0;

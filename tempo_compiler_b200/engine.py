@@ -126,13 +126,15 @@ class Engine:
 
     def _layer(self, lw: LayerWeights, index: int, x, ln, qkv, attn, h, *, decode: bool) -> None:
         ops.layernorm(x, lw.ln1_g, lw.ln1_b, epsilon=LN_EPSILON, out=ln)
-        ops.gemm(ln, lw.w_qkv, bias=lw.b_qkv, out=qkv)
+        # the projection's epilogue also writes this step's keys and values into the layer's cache
         if decode:
-            ops.kv_store(qkv, self.k_cache[index], self.v_cache[index], self.seq_index, self.positions)
+            ops.gemm_qkv(ln, lw.w_qkv, lw.b_qkv, qkv, self.k_cache[index], self.v_cache[index],
+                         positions=self.positions)
             ops.decode_attention(qkv, self.k_cache[index], self.v_cache[index], self.positions, length_offset=1,
                                  out=attn)
         else:
-            ops.kv_store(qkv, self.k_cache[index], self.v_cache[index], self.prompt_seq, self.prompt_pos)
+            ops.gemm_qkv(ln, lw.w_qkv, lw.b_qkv, qkv, self.k_cache[index], self.v_cache[index],
+                         tokens_per_seq=self.prompt)
             ops.attention_prefill(qkv, self.batch, self.prompt, self.shape.heads, out=attn)
         ops.gemm(attn, lw.w_proj, bias=lw.b_proj, residual=x, out=x)
         ops.layernorm(x, lw.ln2_g, lw.ln2_b, epsilon=LN_EPSILON, out=ln)

@@ -56,6 +56,8 @@ _SIGNATURES = {
     "tempo_block_decode_attention": [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp],
     "tempo_block_copy": [_vp, _vp, _u32, _u32, _vp],
     "tempo_gemm": [_vp, _u32, _vp, _u32, _vp, _vp, _u32, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp, _vp],
+    "tempo_gemm_qkv": [_vp, _u32, _vp, _u32, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp,
+                       _vp],
     "tempo_layernorm": [_vp, _u32, _vp, _vp, _vp, _u32, _u32, _f32, _vp],
     "tempo_embed": [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp],
     "tempo_attention_prefill": [_vp, _vp, _u32, _u32, _u32, _u32, _vp],

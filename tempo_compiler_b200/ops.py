@@ -69,6 +69,21 @@ def gemm(a: torch.Tensor, w_t: torch.Tensor, *, bias: torch.Tensor | None = None
     return out
 
 
+def gemm_qkv(a: torch.Tensor, w_t: torch.Tensor, bias: torch.Tensor, out: torch.Tensor, k_cache: torch.Tensor,
+             v_cache: torch.Tensor, *, tokens_per_seq: int = 0, positions: torch.Tensor | None = None) -> torch.Tensor:
+    """The QKV projection (+ bias) into `out`, its key and value columns also stored into the [seq][head][pos][64]
+    caches: row r is sequence r // tokens_per_seq at r % tokens_per_seq, or sequence r at positions[r]."""
+    _check(a, torch.bfloat16, "a")
+    _check(w_t, torch.bfloat16, "w_t")
+    _check(out, torch.bfloat16, "out")
+    m, k = a.shape
+    seqs, heads, capacity, head = k_cache.shape
+    _launch("tempo_gemm_qkv", a.data_ptr(), k, w_t.data_ptr(), k, bias.data_ptr(), out.data_ptr(), out.shape[1], m, k,
+            k_cache.data_ptr(), v_cache.data_ptr(), seqs, heads, head, capacity, tokens_per_seq, _ptr(positions),
+            _stream())
+    return out
+
+
 def gemm_argmax(a: torch.Tensor, w_t: torch.Tensor, part_val: torch.Tensor, part_idx: torch.Tensor) -> None:
     """Per-row (max, first argmax) of a @ w_t^T over each 256-column tile into the partial buffers [M, ceil(N/256)]."""
     _check(a, torch.bfloat16, "a")

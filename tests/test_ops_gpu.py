@@ -182,6 +182,81 @@ def test_gemm_matches_fp32_reference(m: int, n: int, k: int, epilogue: str) -> N
     assert torch.isfinite(out.float()).all()
 
 
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize(("n", "k"), [(2304, 768), (768, 3072), (200, 136)])
+@pytest.mark.parametrize("epilogue", ["bias", "gelu", "residual"])
+def test_gemv_path_for_few_rows_matches_fp32(m: int, n: int, k: int, epilogue: str) -> None:
+    """At most 8 rows take the weight-streaming GEMV kernel; same epilogues, same tolerance."""
+    from tempo_compiler_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(m * 131 + n + k)
+    a = torch.randn((m, k), generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn((n, k), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    residual = torch.randn((m, n), generator=g, device="cuda").to(torch.bfloat16) if epilogue == "residual" else None
+    out = ops.gemm(a, w, bias=bias, residual=residual, gelu=epilogue == "gelu")
+    ref = a.float() @ w.float().T + bias.float()
+    if epilogue == "gelu":
+        ref = torch.nn.functional.gelu(ref.to(torch.bfloat16).float())
+    if residual is not None:
+        ref = ref + residual.float()
+    error = ((out.float() - ref).norm() / ref.norm()).item()
+    assert error < 5e-3, error
+
+
+@pytest.mark.parametrize("m", [1, 3, 8, 200])
+def test_gemm_argmax_small_and_large_batches(m: int) -> None:
+    from tempo_compiler_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(17 + m)
+    a = torch.randn((m, 768), generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn((50257, 768), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    tiles = (50257 + 255) // 256
+    part_val = torch.empty((m, tiles), dtype=torch.float32, device="cuda")
+    part_idx = torch.empty((m, tiles), dtype=torch.int32, device="cuda")
+    ids = torch.empty(m, dtype=torch.int32, device="cuda")
+    ops.gemm_argmax(a, w, part_val, part_idx)
+    ops.argmax_finish(part_val, part_idx, ids)
+    logits = a.float() @ w.float().T
+    top2 = logits.topk(2, dim=1).values
+    clear = (top2[:, 0] - top2[:, 1]) > 1e-3
+    assert torch.equal(ids[clear], logits.argmax(dim=1).to(torch.int32)[clear])
+
+
+@pytest.mark.parametrize(("seqs", "tokens", "decode"), [(3, 40, False), (2, 1000, False), (5, 1, True),
+                                                         (64, 1, True), (300, 1, True)])
+def test_gemm_qkv_writes_keys_and_values_into_the_cache(seqs: int, tokens: int, decode: bool) -> None:
+    """The fused KV write: every row's key and value columns land in the cache exactly as the product computed them,
+    rows past the capacity are skipped, and nothing else in the cache is touched."""
+    from tempo_compiler_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(seqs + tokens)
+    rows = seqs * tokens
+    capacity = 48 if not decode else 16
+    a = torch.randn((rows, 768), generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn((2304, 768), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(2304, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    kc = torch.full((seqs, 12, max(capacity, tokens), 64), 7.0, dtype=torch.bfloat16, device="cuda")
+    vc = torch.full_like(kc, 7.0)
+    capacity = kc.shape[2]
+    out = torch.empty((rows, 2304), dtype=torch.bfloat16, device="cuda")
+    positions = None
+    if decode:
+        positions = torch.randint(0, capacity + 3, (seqs,), generator=g, device="cuda", dtype=torch.int32)
+        ops.gemm_qkv(a, w, bias, out, kc, vc, positions=positions)
+    else:
+        ops.gemm_qkv(a, w, bias, out, kc, vc, tokens_per_seq=tokens)
+    reference = ops.gemm(a, w, bias=bias)
+    assert torch.equal(out, reference)
+    expected_k = torch.full_like(kc, 7.0)
+    expected_v = torch.full_like(vc, 7.0)
+    for r in range(rows):
+        s, p = (r, int(positions[r])) if decode else (r // tokens, r % tokens)
+        if p >= capacity:
+            continue
+        expected_k[s, :, p] = reference[r, 768:1536].view(12, 64)
+        expected_v[s, :, p] = reference[r, 1536:].view(12, 64)
+    assert torch.equal(kc, expected_k)
+    assert torch.equal(vc, expected_v)
+
+
 def test_gemm_argmax_matches_torch() -> None:
     from tempo_compiler_b200 import ops
     g = torch.Generator(device="cuda").manual_seed(5)
