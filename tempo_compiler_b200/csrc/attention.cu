@@ -17,6 +17,16 @@ namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// A 16-byte load of streamed cache data that allocates no L1 line: each key and value is read exactly once, and the
+// SM's L1 may be small when a kernel with a large shared-memory carveout shares the SM.
+__device__ __forceinline__ uint4 ld_stream(const uint4* ptr) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(ptr));
+  return v;
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // Decode
 // ---------------------------------------------------------------------------------------------------------------
@@ -31,20 +41,26 @@ struct DecodeState {
   float m, l, acc[8];
 };
 
-// Folds four keys (scores already in the log2 domain, -inf when absent) into the state.
-__device__ __forceinline__ void fold4(DecodeState& st, const float (&sc)[4], const uint4 (&vv)[4]) {
-  const float mb = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+// Folds KI keys (scores already in the log2 domain, -inf when absent) into the state.
+template <int KI>
+__device__ __forceinline__ void fold(DecodeState& st, const float (&sc)[KI], const uint4 (&vv)[KI]) {
+  float mb = sc[0];
+#pragma unroll
+  for (int i = 1; i < KI; ++i) mb = fmaxf(mb, sc[i]);
   const float m_new = fmaxf(st.m, mb);
   if (m_new == -INFINITY) return;
   const float corr = fast_exp2(st.m - m_new);
-  float pr[4];
+  float pr[KI], psum = 0.f;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) pr[i] = fast_exp2(sc[i] - m_new);
-  st.l = st.l * corr + (pr[0] + pr[1]) + (pr[2] + pr[3]);
+  for (int i = 0; i < KI; ++i) {
+    pr[i] = fast_exp2(sc[i] - m_new);
+    psum += pr[i];
+  }
+  st.l = st.l * corr + psum;
 #pragma unroll
   for (int d = 0; d < 8; ++d) st.acc[d] *= corr;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < KI; ++i) {
     float v[8];
     load8(vv[i], v);
 #pragma unroll
@@ -81,20 +97,39 @@ __device__ __forceinline__ float group_dot(const float (&q)[8], const uint4& k) 
   return s;
 }
 
-// Native decode: one CTA (4 warps) per (head, sequence); caches [seq][head][capacity][64].
+// Native decode over the [seq][head][capacity][64] caches. A cluster of `chunks` CTAs (4 warps each) serves one
+// (head, sequence): CTA c takes a contiguous share of the keys (a multiple of 32), each warp 32 keys per iteration
+// (8 per lane group, 16 independent 16-byte loads in flight per lane). Lane groups and warps merge their online
+// softmax states on the CTA; with chunks > 1 every CTA then stores its (max, sum, 64 weighted values) into the
+// cluster leader's shared memory, and the leader merges them and writes the output. Few sequences therefore still
+// put every SM to work, with no workspace and no second kernel.
+constexpr int kDecodeKeys = 8;                       // keys per lane group per iteration
+constexpr int kDecodeWarpKeys = 4 * kDecodeKeys;     // keys per warp per iteration
+constexpr uint32_t kDecodeMaxChunks = 8;
+
+__device__ __forceinline__ uint32_t decode_cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
 __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* __restrict__ qkv,
                                                                const uint16_t* __restrict__ k_cache,
                                                                const uint16_t* __restrict__ v_cache,
                                                                const int32_t* __restrict__ lengths,
                                                                int32_t length_offset, uint16_t* __restrict__ out,
-                                                               uint32_t heads, uint32_t capacity) {
-  pdl_launch_dependents();
+                                                               uint32_t heads, uint32_t capacity, uint32_t early) {
+  if (early) pdl_launch_dependents();
   pdl_wait();
-  const uint32_t h = blockIdx.x, s = blockIdx.y;
+  const uint32_t chunks = gridDim.x, h = blockIdx.y, s = blockIdx.z;
+  const uint32_t chunk = chunks > 1 ? decode_cluster_rank() : 0u;
   const uint32_t warp = warp_id(), lane = lane_id();
   const uint32_t g = lane >> 3, li = lane & 7u;
   const uint32_t width = heads * 64;
   const int32_t len = max(0, min(lengths[s] + length_offset, int32_t(capacity)));
+  const int32_t per = ((len + int32_t(chunks) - 1) / int32_t(chunks) + 31) & ~31;
+  const int32_t k_begin = min(len, int32_t(chunk) * per);
+  const int32_t k_end = min(len, k_begin + per);
   float q[8];
   load8(reinterpret_cast<const uint4*>(qkv + size_t(s) * 3 * width + h * 64)[li], q);
 #pragma unroll
@@ -106,41 +141,44 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* _
   st.l = 0.f;
 #pragma unroll
   for (int d = 0; d < 8; ++d) st.acc[d] = 0.f;
-  for (int32_t base = int32_t(warp) * 16; base < len; base += 64) {
-    uint4 kk[4], vv[4];
+  for (int32_t base = k_begin + int32_t(warp) * kDecodeWarpKeys; base < k_end; base += 4 * kDecodeWarpKeys) {
+    uint4 kk[kDecodeKeys], vv[kDecodeKeys];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kDecodeKeys; ++i) {
       const int32_t key = base + i * 4 + int32_t(g);
-      if (key < len) {
-        kk[i] = __ldg(kb4 + size_t(key) * 8 + li);
-        vv[i] = __ldg(vb4 + size_t(key) * 8 + li);
+      if (key < k_end) {
+        kk[i] = ld_stream(kb4 + size_t(key) * 8 + li);
+        vv[i] = ld_stream(vb4 + size_t(key) * 8 + li);
       } else {
         kk[i] = make_uint4(0, 0, 0, 0);
         vv[i] = make_uint4(0, 0, 0, 0);
       }
     }
-    float sc[4];
+    float sc[kDecodeKeys];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < kDecodeKeys; ++i) {
       const float v = group_dot(q, kk[i]);
-      sc[i] = (base + i * 4 + int32_t(g) < len) ? v : -INFINITY;
+      sc[i] = (base + i * 4 + int32_t(g) < k_end) ? v : -INFINITY;
     }
-    fold4(st, sc, vv);
+    fold<kDecodeKeys>(st, sc, vv);
   }
+  // A grid of several waves lets the next kernel start its prologue only now: a trigger at entry would let that
+  // kernel's CTAs take SM resources while later waves of this grid still wait to be scheduled.
+  if (!early) pdl_launch_dependents();
   merge_shfl(st, 8);
   merge_shfl(st, 16);
   __shared__ float sm_m[4], sm_l[4], sm_acc[4][64];
+  __shared__ float part[kDecodeMaxChunks][66];  // the leader's: per CTA of the cluster, (max, sum, 64 values)
   if (g == 0) {
 #pragma unroll
     for (int d = 0; d < 8; ++d) sm_acc[warp][li * 8 + d] = st.acc[d];
     if (li == 0) { sm_m[warp] = st.m; sm_l[warp] = st.l; }
   }
   __syncthreads();
-  if (threadIdx.x < 64) {
-    const uint32_t d = threadIdx.x;
-    float m = -INFINITY;
+  const uint32_t d = threadIdx.x;
+  float m = -INFINITY, l = 0.f, a = 0.f;
+  if (d < 64) {
     for (int w = 0; w < 4; ++w) m = fmaxf(m, sm_m[w]);
-    float l = 0.f, a = 0.f;
     if (m != -INFINITY) {
       for (int w = 0; w < 4; ++w) {
         const float f = fast_exp2(sm_m[w] - m);
@@ -148,7 +186,33 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* _
         a += sm_acc[w][d] * f;
       }
     }
-    out[size_t(s) * width + h * 64 + d] = float_to_bf16(l > 0.f ? a / l : 0.f);
+  }
+  if (chunks == 1) {
+    if (d < 64) out[size_t(s) * width + h * 64 + d] = float_to_bf16(l > 0.f ? a / l : 0.f);
+    return;
+  }
+  if (d < 64) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(&part[chunk][0])), "r"(0u));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote + (2 + d) * 4), "f"(a) : "memory");
+    if (d == 0) {
+      asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(m) : "memory");
+      asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote + 4), "f"(l) : "memory");
+    }
+  }
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (chunk == 0 && d < 64) {
+    float mm = -INFINITY;
+    for (uint32_t c = 0; c < chunks; ++c) mm = fmaxf(mm, part[c][0]);
+    float ll = 0.f, aa = 0.f;
+    if (mm != -INFINITY) {
+      for (uint32_t c = 0; c < chunks; ++c) {
+        const float f = fast_exp2(part[c][0] - mm);
+        ll += part[c][1] * f;
+        aa += part[c][2 + d] * f;
+      }
+    }
+    out[size_t(s) * width + h * 64 + d] = float_to_bf16(ll > 0.f ? aa / ll : 0.f);
   }
 }
 
@@ -189,7 +253,7 @@ __global__ void __launch_bounds__(128) block_decode_kernel(const uint16_t* __res
     float sc[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) sc[i] = group_dot(q, kk[i]) + mk[i] * kLog2e;
-    fold4(st, sc, vv);
+    fold<4>(st, sc, vv);
   }
   merge_shfl(st, 8);
   merge_shfl(st, 16);
@@ -230,13 +294,19 @@ extern "C" tempo_status tempo_decode_attention(const void* qkv, const void* k_ca
                                                const int32_t* lengths, int32_t length_offset, void* out,
                                                uint32_t seqs, uint32_t heads, uint32_t head, uint32_t capacity,
                                                void* stream) {
-  if (seqs == 0 || heads == 0 || head != 64 || capacity == 0)
+  if (seqs == 0 || heads == 0 || head != 64 || capacity == 0 || seqs > 65535 || heads > 65535)
     return fail(TEMPO_ERR_VALUE, "tempo_decode_attention: seqs %u heads %u head %u capacity %u", seqs, heads, head,
                 capacity);
   if (!aligned16(qkv) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
     return fail(TEMPO_ERR_VALUE, "tempo_decode_attention: operands must be 16-byte aligned");
-  return launch(decode_attention_kernel, dim3(heads, seqs), dim3(128), 0, static_cast<cudaStream_t>(stream), 1,
-                "decode_attention_kernel", static_cast<const uint16_t*>(qkv), static_cast<const uint16_t*>(k_cache),
-                static_cast<const uint16_t*>(v_cache), lengths, length_offset, static_cast<uint16_t*>(out), heads,
-                capacity);
+  // Fewer (sequence, head) pairs than SMs (a handful of sequences): split each over up to eight CTAs of a cluster,
+  // each with at least 128 keys of the capacity, until every SM has one. Larger batches keep one CTA per pair: the
+  // cluster merge costs more than the parallelism it adds once every SM is busy.
+  const uint64_t pairs = uint64_t(seqs) * heads, target = uint64_t(sm_count());
+  uint32_t chunks = 1;
+  while (chunks < kDecodeMaxChunks && pairs * chunks < target && capacity >= 2 * 128 * chunks) chunks *= 2;
+  return launch(decode_attention_kernel, dim3(chunks, heads, seqs), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                chunks, "decode_attention_kernel", static_cast<const uint16_t*>(qkv),
+                static_cast<const uint16_t*>(k_cache), static_cast<const uint16_t*>(v_cache), lengths, length_offset,
+                static_cast<uint16_t*>(out), heads, capacity, single_wave(pairs * chunks, 4));
 }

@@ -1,20 +1,22 @@
 // Causal prefill attention on the 5th-generation tensor cores (flash-attention tile loop, one CTA per 128 queries of
 // one head of one sequence, two CTAs per SM).
 //
-//   warp 0      TMA: Q once, then K and V 128 keys at a time into a two-stage ring.
-//   warp 1      MMA issuer and TMEM owner: S = Q K^T into TMEM (128 columns, FP32); after the softmax has written P
-//               over S, O += P V with P read straight from TMEM (A operand in tensor memory) and V from shared memory;
-//               O stays in TMEM (64 columns) for the whole key loop.
-//   warps 2-5   softmax, one query row per thread: read S, mask (diagonal tile only), exp2 on the special-function
-//               unit, P as BF16 pairs into TMEM, the row sum in FP32. The exponent base only moves when the row
-//               maximum grows by more than 2^8; only then are O and the sum rescaled (in TMEM), which keeps the math
-//               exact while skipping almost every rescale. At the end O / sum is written out.
+//   warp 0      TMA: Q once, then K and V 64 keys at a time into a four-stage ring.
+//   warp 1      MMA issuer and TMEM owner. S = Q K^T goes into one of two 64-column TMEM buffers (FP32), so the
+//               product of the next key tile runs while the softmax works on this one; after the softmax has written
+//               P over its S, O += P V with P read straight from TMEM (A operand in tensor memory) and V from shared
+//               memory. O stays in TMEM (64 columns) for the whole key loop.
+//   warps 2-5   softmax, one query row per thread: read S, mask (tiles reaching past the tile's first query only),
+//               exp2 on the special-function unit, P as BF16 pairs into TMEM, the row sum in FP32. The exponent base
+//               only moves when the row maximum grows by more than 2^8; only then are O and the sum rescaled (in
+//               TMEM), which keeps the math exact while skipping almost every rescale. At the end O / sum is written.
 //
 // Two source layouts share the kernel:
 //   PACKED    the drop-in fused QKV tensor, per 32-token block a 512-byte zero tile then [3*heads*4][32][16]
-//             (attention, board_package/gpt2_inference.py:981-1003; tempo_ops.td:292-314). A 4-D tensor map
-//             (16, 32 tokens, blocks, 16-wide feature tiles) loads 4 blocks x 4 tiles, which lands as four 128-row
-//             K-major 32-byte-swizzled tiles: exactly the MMA operand layout. The output overwrites the queries.
+//             (attention, board_package/gpt2_inference.py:981-1003; tempo_ops.td:292-314). 4-D tensor maps
+//             (16, 32 tokens, blocks, 16-wide feature tiles) load 4 (queries) or 2 (keys, values) blocks x 4 tiles,
+//             which land as 128- or 64-row K-major 32-byte-swizzled tiles: exactly the MMA operand layout. The output
+//             overwrites the queries.
 //   ROWMAJOR  the native engine's qkv [seqs*tokens, 3*heads*64], 128-byte swizzle, output to its own buffer.
 // Queries arrive scaled by 1/sqrt(head) (folded into the QKV weights, gpt2_inference.py:1153-1168).
 #include <cuda.h>
@@ -32,23 +34,30 @@ namespace {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only when the maximum grows by more than 2^8
 constexpr int kThreads = 192;
-constexpr uint32_t kTileBytes = 128 * 64 * 2;  // one 128 x 64 BF16 operand tile
+constexpr uint32_t kKeys = 64;                        // keys per K/V tile
+constexpr uint32_t kStages = 4;                       // K/V ring depth
+constexpr uint32_t kQBytes = 128 * 64 * 2;            // one 128-query x 64-dim BF16 tile
+constexpr uint32_t kKvTileBytes = kKeys * 64 * 2;     // one 64-key x 64-dim BF16 tile
 
 struct PrefillParams {
   uint16_t* out;         // ROWMAJOR: [seqs*tokens, heads*64]; PACKED: the fused tensor (queries overwritten)
   uint32_t seqs, tokens, heads;
   uint32_t q_tiles;      // ceil(tokens / 128)
   uint64_t block_bytes;  // PACKED: bytes per 32-token block of the fused tensor
+  uint32_t early;        // the grid fits in one wave: dependents may launch at entry
 };
 
-// Shared memory: Q | K[2] | V[2] | barriers.
+// Shared memory: Q | K[kStages] | V[kStages] | barriers.
 constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kTileBytes;
-constexpr uint32_t kOffV = 3 * kTileBytes;
-constexpr uint32_t kOffBar = 5 * kTileBytes;
-// q_full, kv_full[2], kv_empty[2], s_full, p_full, o_full, final
-constexpr uint32_t kBarCount = 9;
+constexpr uint32_t kOffK = kQBytes;
+constexpr uint32_t kOffV = kOffK + kStages * kKvTileBytes;
+constexpr uint32_t kOffBar = kOffV + kStages * kKvTileBytes;
+// q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full, final
+constexpr uint32_t kBarCount = 1 + 2 * kStages + 2 + 2 + 1 + 1;
 constexpr uint32_t kSmem = kOffBar + kBarCount * 8 + 16 + 1024;
+
+// TMEM columns: S/P buffer 0 | S/P buffer 1 | O.
+constexpr uint32_t kTmemS0 = 0, kTmemS1 = 64, kTmemO = 128, kTmemCols = 256;
 
 template <bool PACKED>
 __device__ __forceinline__ void load_tile(void* dst, const CUtensorMap* map, uint64_t* bar, uint32_t feature_tile16,
@@ -60,119 +69,135 @@ __device__ __forceinline__ void load_tile(void* dst, const CUtensorMap* map, uin
   }
 }
 
-// Descriptor of the kk-th 16-deep K-major slice of a 128-row operand tile.
+// Descriptor of the kk-th 16-deep K-major slice of a `rows`-row operand tile.
 template <bool PACKED>
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, uint32_t kk) {
-  if constexpr (PACKED) return make_smem_desc(tile_addr + kk * 4096, 16, 256, kLayoutSw32);
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, uint32_t kk, uint32_t rows) {
+  if constexpr (PACKED) return make_smem_desc(tile_addr + kk * rows * 32, 16, 256, kLayoutSw32);
   else return make_smem_desc(tile_addr + kk * 32, 16, 1024, kLayoutSw128);
 }
 
-// Descriptor of the kk-th 16-key slice of V as the MN-major B operand (N = 64 head dims).
+// Descriptor of the kk-th 16-key slice of a 64-key V tile as the MN-major B operand (N = 64 head dims).
 template <bool PACKED>
 __device__ __forceinline__ uint64_t v_desc(uint32_t tile_addr, uint32_t kk) {
-  if constexpr (PACKED) return make_smem_desc(tile_addr + kk * 512, 4096, 256, kLayoutSw32);
+  if constexpr (PACKED) return make_smem_desc(tile_addr + kk * 512, kKeys * 32, 256, kLayoutSw32);
   else return make_smem_desc(tile_addr + kk * 2048, 8192, 1024, kLayoutSw128);
 }
 
 template <bool PACKED>
 __global__ void __launch_bounds__(kThreads, 2)
-    attention_prefill_kernel(const __grid_constant__ CUtensorMap tmap, PrefillParams p) {
+    attention_prefill_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_kv,
+                             PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 3;
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* o_full = bars + 7;
-  uint64_t* final_bar = bars + 8;
+  uint64_t* kv_empty = bars + 1 + kStages;
+  uint64_t* s_full = bars + 1 + 2 * kStages;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_full = p_full + 2;
+  uint64_t* final_bar = o_full + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBarCount);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  // Heaviest query tiles first (causal: tile qt reads qt+1 key tiles).
+  // Heaviest query tiles first (causal: tile qt reads about 2(qt+1) key tiles).
   const uint32_t qt = p.q_tiles - 1 - (blockIdx.x % p.q_tiles);
   const uint32_t h = (blockIdx.x / p.q_tiles) % p.heads;
   const uint32_t s = blockIdx.x / (p.q_tiles * p.heads);
-  const uint32_t kv_tiles = qt + 1;
+  const uint32_t last_query = min(p.tokens, (qt + 1) * 128) - 1;
+  const uint32_t kv_tiles = last_query / kKeys + 1;
+  const uint32_t first_masked = (qt * 128) / kKeys;  // key tiles from here on reach past the tile's first query
   const uint32_t warp = warp_id(), lane = lane_id();
   const uint32_t heads4 = p.heads * 4;  // 16-wide feature tiles per third of the fused tensor
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (uint32_t i = 0; i < kStages; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+    }
     mbar_init(o_full, 1);
     mbar_init(final_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
-    tma_prefetch_desc(&tmap);
+    tma_prefetch_desc(&tmap_q);
+    tma_prefetch_desc(&tmap_kv);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tmem_s = tmem_base;        // 128 columns: S (FP32), then P (BF16 pairs) in its first 64
-  const uint32_t tmem_o = tmem_base + 128;  // 64 columns: O (FP32)
-  pdl_launch_dependents();
+  if (p.early) pdl_launch_dependents();
   pdl_wait();  // Q, K and V are the previous kernel's output
 
-  auto tile_coord = [&](uint32_t t) -> int32_t {
-    if constexpr (PACKED) return int32_t(t * 4);
-    else return int32_t(s * p.tokens + t * 128);
+  auto q_coord = [&]() -> int32_t {
+    if constexpr (PACKED) return int32_t(qt * 4);
+    else return int32_t(s * p.tokens + qt * 128);
+  };
+  auto kv_coord = [&](uint32_t j) -> int32_t {
+    if constexpr (PACKED) return int32_t(j * 2);
+    else return int32_t(s * p.tokens + j * kKeys);
   };
 
   if (warp == 0) {
     if (elect_one()) {
-      bool issued[2] = {false, false};
-      uint32_t parity_of[2] = {0, 0};
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      load_tile<PACKED>(smem + kOffQ, &tmap, q_full, h * 4, tile_coord(qt));
+      bool issued[kStages];
+      uint32_t parity_of[kStages];
+      for (uint32_t i = 0; i < kStages; ++i) { issued[i] = false; parity_of[i] = 0; }
+      mbar_arrive_expect_tx(q_full, kQBytes);
+      load_tile<PACKED>(smem + kOffQ, &tmap_q, q_full, h * 4, q_coord());
       for (uint32_t j = 0; j < kv_tiles; ++j) {
-        const uint32_t st = j & 1u, ph = (j >> 1) & 1u;
+        const uint32_t st = j % kStages, ph = (j / kStages) & 1u;
         if (!mbar_wait(&kv_empty[st], ph ^ 1u, kWatchEmpty, abort_flag)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
-        load_tile<PACKED>(smem + kOffK + st * kTileBytes, &tmap, &kv_full[st], heads4 + h * 4, tile_coord(j));
-        load_tile<PACKED>(smem + kOffV + st * kTileBytes, &tmap, &kv_full[st], 2 * heads4 + h * 4, tile_coord(j));
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kKvTileBytes);
+        load_tile<PACKED>(smem + kOffK + st * kKvTileBytes, &tmap_kv, &kv_full[st], heads4 + h * 4, kv_coord(j));
+        load_tile<PACKED>(smem + kOffV + st * kKvTileBytes, &tmap_kv, &kv_full[st], 2 * heads4 + h * 4, kv_coord(j));
         issued[st] = true;
         parity_of[st] = ph;
       }
       mbar_wait(q_full, 0, kWatchFull, nullptr);
-      for (int i = 0; i < 2; ++i)
+      for (uint32_t i = 0; i < kStages; ++i)
         if (issued[i]) mbar_wait(&kv_full[i], parity_of[i], kWatchFull, nullptr);
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idesc_s = make_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idesc_s = make_idesc_bf16(128, kKeys, 0, 0);
       constexpr uint32_t idesc_o = make_idesc_bf16(128, 64, 0, 1);
       const uint32_t q_addr = smem_u32(smem + kOffQ);
-      bool ok = mbar_wait(q_full, 0, kWatchFull, abort_flag);
-      for (uint32_t j = 0; j < kv_tiles && ok; ++j) {
-        const uint32_t st = j & 1u, ph = (j >> 1) & 1u;
-        if (!mbar_wait(&kv_full[st], ph, kWatchFull, abort_flag)) break;
+      // S_j = Q K_j^T into buffer j & 1. The buffer held P_{j-2}, whose P V was issued before (issue order).
+      auto issue_s = [&](uint32_t j) -> bool {
+        const uint32_t st = j % kStages;
+        if (!mbar_wait(&kv_full[st], (j / kStages) & 1u, kWatchFull, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + kOffK + st * kTileBytes);
-        const uint32_t v_addr = smem_u32(smem + kOffV + st * kTileBytes);
-        // S overwrites the P of the previous tile, which the P V issued just before has read (issue order).
+        const uint32_t k_addr = smem_u32(smem + kOffK + st * kKvTileBytes);
+        const uint32_t d = tmem_base + ((j & 1u) ? kTmemS1 : kTmemS0);
 #pragma unroll
         for (uint32_t kk = 0; kk < 4; ++kk)
-          umma_bf16(tmem_s, kmajor_desc<PACKED>(q_addr, kk), kmajor_desc<PACKED>(k_addr, kk), idesc_s, kk != 0);
-        umma_commit(s_full);
-        if (!mbar_wait(p_full, j & 1u, kWatchOther, abort_flag)) break;
+          umma_bf16(d, kmajor_desc<PACKED>(q_addr, kk, 128), kmajor_desc<PACKED>(k_addr, kk, kKeys), idesc_s,
+                    kk != 0);
+        umma_commit(&s_full[j & 1u]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, kWatchFull, abort_flag) && issue_s(0);
+      for (uint32_t j = 0; j < kv_tiles && ok; ++j) {
+        if (j + 1 < kv_tiles && !issue_s(j + 1)) break;
+        if (!mbar_wait(&p_full[j & 1u], (j >> 1) & 1u, kWatchOther, abort_flag)) break;
         tc_fence_after();
+        const uint32_t v_addr = smem_u32(smem + kOffV + (j % kStages) * kKvTileBytes);
+        const uint32_t pa = tmem_base + ((j & 1u) ? kTmemS1 : kTmemS0);
 #pragma unroll
-        for (uint32_t kk = 0; kk < 8; ++kk)
-          umma_bf16_tmem_a(tmem_o, tmem_s + kk * 8, v_desc<PACKED>(v_addr, kk), idesc_o, (j | kk) != 0u);
+        for (uint32_t kk = 0; kk < kKeys / 16; ++kk)
+          umma_bf16_tmem_a(tmem_base + kTmemO, pa + kk * 8, v_desc<PACKED>(v_addr, kk), idesc_o, (j | kk) != 0u);
         umma_commit(o_full);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&kv_empty[j % kStages]);
       }
       umma_commit(final_bar);
       mbar_wait(final_bar, 0, kWatchOther, nullptr);
@@ -182,59 +207,53 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t row = lane_base + lane;
     const uint32_t q_local = qt * 128 + row;  // query position in the sequence
     const uint32_t lane_addr = lane_base << 16;
-    float m_used = -INFINITY, l = 0.f;
+    const uint32_t tmem_o = tmem_base + kTmemO;
+    float m_used = -INFINITY, l = 0.f;  // m_used: raw-score units
     bool ok = true;
     for (uint32_t j = 0; j < kv_tiles; ++j) {
-      if (!mbar_wait(s_full, j & 1u, kWatchOther, abort_flag)) { ok = false; break; }
+      const uint32_t buf = tmem_base + ((j & 1u) ? kTmemS1 : kTmemS0);
+      if (!mbar_wait(&s_full[j & 1u], (j >> 1) & 1u, kWatchOther, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      uint32_t sr[128];
-      tmem_ld_32x32b_x32(tmem_s + lane_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(sr + 0));
-      tmem_ld_32x32b_x32(tmem_s + lane_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-      tmem_ld_32x32b_x32(tmem_s + lane_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
-      tmem_ld_32x32b_x32(tmem_s + lane_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
+      uint32_t sr[kKeys];
+      tmem_ld_32x32b_x32(buf + lane_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(sr + 0));
+      tmem_ld_32x32b_x32(buf + lane_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
       tmem_wait_ld();
       float mx = -INFINITY;
-      if (j == qt) {
-        // Diagonal tile: keys past the query, and past the sequence end, are masked.
+      if (j >= first_masked) {
+        // Keys past the query, and past the sequence end, are masked.
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const uint32_t key = j * 128 + c;
-          float v = __uint_as_float(sr[c]) * kLog2e;
-          if (key > q_local || key >= p.tokens) v = -INFINITY;
-          sr[c] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
+        for (uint32_t c = 0; c < kKeys; ++c) {
+          const uint32_t key = j * kKeys + c;
+          if (key > q_local || key >= p.tokens) sr[c] = __float_as_uint(-INFINITY);
+          mx = fmaxf(mx, __uint_as_float(sr[c]));
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const float v = __uint_as_float(sr[c]) * kLog2e;
-          sr[c] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
-        }
+        for (uint32_t c = 0; c < kKeys; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
       }
       bool rescale = false;
       float factor = 1.f;
-      if (j == 0) {
+      if (m_used == -INFINITY) {
         m_used = mx;
-      } else if (mx > m_used + kRescaleThreshold) {
-        factor = fast_exp2(m_used - mx);
+      } else if ((mx - m_used) * kLog2e > kRescaleThreshold) {
+        factor = fast_exp2((m_used - mx) * kLog2e);
         m_used = mx;
         l *= factor;
         rescale = true;
       }
-      const float base = m_used == -INFINITY ? 0.f : m_used;
+      const float base = m_used == -INFINITY ? 0.f : m_used * kLog2e;
       float sum = 0.f;
 #pragma unroll
-      for (int c16 = 0; c16 < 4; ++c16) {
+      for (int c16 = 0; c16 < int(kKeys / 32); ++c16) {
         uint32_t packed[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float e0 = fast_exp2(__uint_as_float(sr[c16 * 32 + 2 * i]) - base);
-          const float e1 = fast_exp2(__uint_as_float(sr[c16 * 32 + 2 * i + 1]) - base);
+          const float e0 = fast_exp2(fmaf(__uint_as_float(sr[c16 * 32 + 2 * i]), kLog2e, -base));
+          const float e1 = fast_exp2(fmaf(__uint_as_float(sr[c16 * 32 + 2 * i + 1]), kLog2e, -base));
           sum += e0 + e1;
           packed[i] = pack_bf16x2(e0, e1);
         }
-        tmem_st_32x32b_x16(tmem_s + lane_addr + c16 * 16, packed);
+        tmem_st_32x32b_x16(buf + lane_addr + c16 * 16, packed);
       }
       l += sum;
       // The rescale must wait for the previous P V (the only MMA writing O) to finish.
@@ -261,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[j & 1u]);
       if (!ok) break;
     }
     if (ok && mbar_wait(o_full, (kv_tiles - 1) & 1u, kWatchOther, abort_flag)) {
@@ -300,11 +319,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   }
 
+  // A grid of several waves lets dependents start only as its last wave drains, so they take no SM a later CTA of
+  // this grid needs.
+  if (!p.early) pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 256);
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -321,13 +343,17 @@ extern "C" tempo_status tempo_block_attention(const void* constants, void* fused
                 heads, head);
   if (!aligned16(fused)) return fail(TEMPO_ERR_VALUE, "tempo_block_attention: fused tensor must be 16-byte aligned");
   const uint64_t block_bytes = 512 + 32ull * 3 * heads * head * 2;
-  CUtensorMap map;
-  // The queries pointer is past block 0's zero tile; the map addresses every block's tiles from there.
+  CUtensorMap map_q, map_kv;
+  // The queries pointer is past block 0's zero tile; the maps address every block's tiles from there.
   const uint64_t dims[4] = {16, 32, tokens / 32, 3ull * heads * 4};
   const uint64_t strides[3] = {32, block_bytes, 1024};
-  const uint32_t box[4] = {16, 32, 4, 4};
-  tempo_status s = encode_tmap(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, fused, dims, strides, box,
+  const uint32_t box_q[4] = {16, 32, 4, 4};
+  const uint32_t box_kv[4] = {16, 32, kKeys / 32, 4};
+  tempo_status s = encode_tmap(&map_q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, fused, dims, strides, box_q,
                                CU_TENSOR_MAP_SWIZZLE_32B);
+  if (s != TEMPO_OK) return s;
+  s = encode_tmap(&map_kv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, fused, dims, strides, box_kv,
+                  CU_TENSOR_MAP_SWIZZLE_32B);
   if (s != TEMPO_OK) return s;
   PrefillParams p{};
   p.out = static_cast<uint16_t*>(fused);
@@ -336,9 +362,10 @@ extern "C" tempo_status tempo_block_attention(const void* constants, void* fused
   p.heads = heads;
   p.q_tiles = (tokens + 127) / 128;
   p.block_bytes = block_bytes;
+  p.early = single_wave(uint64_t(p.q_tiles) * heads, 2);
   if ((s = set_smem(reinterpret_cast<const void*>(attention_prefill_kernel<true>), kSmem))) return s;
   return launch(attention_prefill_kernel<true>, dim3(p.q_tiles * heads), dim3(kThreads), kSmem,
-                static_cast<cudaStream_t>(stream), 1, "attention_prefill_kernel<packed>", map, p);
+                static_cast<cudaStream_t>(stream), 1, "attention_prefill_kernel<packed>", map_q, map_kv, p);
 }
 
 extern "C" tempo_status tempo_attention_prefill(const void* qkv, void* out, uint32_t seqs, uint32_t tokens,
@@ -348,12 +375,16 @@ extern "C" tempo_status tempo_attention_prefill(const void* qkv, void* out, uint
                 heads, head);
   if (!aligned16(qkv) || !aligned16(out))
     return fail(TEMPO_ERR_VALUE, "tempo_attention_prefill: operands must be 16-byte aligned");
-  CUtensorMap map;
+  CUtensorMap map_q, map_kv;
   const uint64_t dims[2] = {3ull * heads * head, uint64_t(seqs) * tokens};
   const uint64_t strides[1] = {3ull * heads * head * 2};
-  const uint32_t box[2] = {64, 128};
-  tempo_status s = encode_tmap(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv, dims, strides, box,
+  const uint32_t box_q[2] = {64, 128};
+  const uint32_t box_kv[2] = {64, kKeys};
+  tempo_status s = encode_tmap(&map_q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv, dims, strides, box_q,
                                CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != TEMPO_OK) return s;
+  s = encode_tmap(&map_kv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, qkv, dims, strides, box_kv,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
   if (s != TEMPO_OK) return s;
   PrefillParams p{};
   p.out = static_cast<uint16_t*>(out);
@@ -363,7 +394,8 @@ extern "C" tempo_status tempo_attention_prefill(const void* qkv, void* out, uint
   p.q_tiles = (tokens + 127) / 128;
   const uint64_t ctas = uint64_t(p.q_tiles) * heads * seqs;
   if (ctas > 0x7FFFFFFFull) return fail(TEMPO_ERR_VALUE, "tempo_attention_prefill: too many tiles");
+  p.early = single_wave(ctas, 2);
   if ((s = set_smem(reinterpret_cast<const void*>(attention_prefill_kernel<false>), kSmem))) return s;
   return launch(attention_prefill_kernel<false>, dim3(uint32_t(ctas)), dim3(kThreads), kSmem,
-                static_cast<cudaStream_t>(stream), 1, "attention_prefill_kernel<rowmajor>", map, p);
+                static_cast<cudaStream_t>(stream), 1, "attention_prefill_kernel<rowmajor>", map_q, map_kv, p);
 }

@@ -99,8 +99,9 @@ __global__ void block_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __re
 template <int CPL>
 __global__ void layernorm_kernel(const uint16_t* __restrict__ x, uint32_t x_stride,
                                  const uint16_t* __restrict__ gamma, const uint16_t* __restrict__ beta,
-                                 uint16_t* __restrict__ out, uint32_t rows, uint32_t features, float epsilon) {
-  pdl_launch_dependents();
+                                 uint16_t* __restrict__ out, uint32_t rows, uint32_t features, float epsilon,
+                                 uint32_t early) {
+  if (early) pdl_launch_dependents();
   pdl_wait();
   const uint32_t row = blockIdx.x * (blockDim.x / 32) + warp_id();
   if (row >= rows) return;
@@ -142,14 +143,15 @@ __global__ void layernorm_kernel(const uint16_t* __restrict__ x, uint32_t x_stri
       *reinterpret_cast<uint4*>(orow + c * 8) = pack8(v[i]);
     }
   }
+  if (!early) pdl_launch_dependents();
 }
 
 // ---- embedding gather: x[r] = round(wte[ids[r]] + wpe[pos[r]]) ----
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ positions,
                              const uint16_t* __restrict__ wte, const uint16_t* __restrict__ wpe,
                              uint16_t* __restrict__ x, uint32_t rows, uint32_t width, uint32_t vocab,
-                             uint32_t max_positions) {
-  pdl_launch_dependents();
+                             uint32_t max_positions, uint32_t early) {
+  if (early) pdl_launch_dependents();
   pdl_wait();
   const uint32_t per_row = width / 8;
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -165,14 +167,15 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const int32_t* __r
 #pragma unroll
   for (int j = 0; j < 8; ++j) a[j] += b[j];
   reinterpret_cast<uint4*>(x + size_t(r) * width)[c] = pack8(a);
+  if (!early) pdl_launch_dependents();
 }
 
 // ---- KV store: keys and values of qkv rows into [seq][head][capacity][head_dim] caches ----
 __global__ void kv_store_kernel(const uint16_t* __restrict__ qkv, uint16_t* __restrict__ k_cache,
                                 uint16_t* __restrict__ v_cache, const int32_t* __restrict__ seq_of,
                                 const int32_t* __restrict__ pos_of, uint32_t rows, uint32_t seqs, uint32_t heads,
-                                uint32_t head, uint32_t capacity) {
-  pdl_launch_dependents();
+                                uint32_t head, uint32_t capacity, uint32_t early) {
+  if (early) pdl_launch_dependents();
   pdl_wait();
   const uint32_t width = heads * head;
   const uint32_t per_row = 2 * width / 8;  // 16-byte vectors of keys then values
@@ -187,6 +190,7 @@ __global__ void kv_store_kernel(const uint16_t* __restrict__ qkv, uint16_t* __re
   uint16_t* cache = which ? v_cache : k_cache;
   const size_t slot = ((size_t(seq_of[r]) * heads + h) * capacity + size_t(pos_of[r])) * head + d;
   *reinterpret_cast<uint4*>(cache + slot) = w;
+  if (!early) pdl_launch_dependents();
 }
 
 // ---- argmax reduction over the LM head's per-tile partials; first index wins ties ----
@@ -280,7 +284,8 @@ extern "C" tempo_status tempo_layernorm(const void* x, uint32_t x_stride, const 
               : cpl <= 4 ? layernorm_kernel<4>
               : cpl <= 8 ? layernorm_kernel<8>
                          : layernorm_kernel<16>;
-  return launch(kernel, grid, block, 0, st, 1, "layernorm_kernel", xs, x_stride, gs, bs, os, rows, features, epsilon);
+  return launch(kernel, grid, block, 0, st, 1, "layernorm_kernel", xs, x_stride, gs, bs, os, rows, features, epsilon,
+                single_wave(grid.x, 8));
 }
 
 extern "C" tempo_status tempo_embed(const int32_t* ids, const int32_t* positions, const void* wte, const void* wpe,
@@ -290,9 +295,10 @@ extern "C" tempo_status tempo_embed(const int32_t* ids, const int32_t* positions
   if (!aligned16(wte) || !aligned16(wpe) || !aligned16(x))
     return fail(TEMPO_ERR_VALUE, "tempo_embed: operands must be 16-byte aligned");
   const uint64_t threads = uint64_t(rows) * (width / 8);
-  return launch(embed_kernel, dim3(uint32_t((threads + 255) / 256)), dim3(256), 0, static_cast<cudaStream_t>(stream),
-                1, "embed_kernel", ids, positions, static_cast<const uint16_t*>(wte),
-                static_cast<const uint16_t*>(wpe), static_cast<uint16_t*>(x), rows, width, vocab, max_positions);
+  const uint32_t blocks = uint32_t((threads + 255) / 256);
+  return launch(embed_kernel, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream), 1, "embed_kernel", ids,
+                positions, static_cast<const uint16_t*>(wte), static_cast<const uint16_t*>(wpe),
+                static_cast<uint16_t*>(x), rows, width, vocab, max_positions, single_wave(blocks, 8));
 }
 
 extern "C" tempo_status tempo_kv_store(const void* qkv, void* k_cache, void* v_cache, const int32_t* seq_of,
@@ -303,9 +309,10 @@ extern "C" tempo_status tempo_kv_store(const void* qkv, void* k_cache, void* v_c
   if (!aligned16(qkv) || !aligned16(k_cache) || !aligned16(v_cache))
     return fail(TEMPO_ERR_VALUE, "tempo_kv_store: operands must be 16-byte aligned");
   const uint64_t threads = uint64_t(rows) * (2 * heads * head / 8);
-  return launch(kv_store_kernel, dim3(uint32_t((threads + 255) / 256)), dim3(256), 0, static_cast<cudaStream_t>(stream),
-                1, "kv_store_kernel", static_cast<const uint16_t*>(qkv), static_cast<uint16_t*>(k_cache),
-                static_cast<uint16_t*>(v_cache), seq_of, pos_of, rows, seqs, heads, head, capacity);
+  const uint32_t blocks = uint32_t((threads + 255) / 256);
+  return launch(kv_store_kernel, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream), 1, "kv_store_kernel",
+                static_cast<const uint16_t*>(qkv), static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache),
+                seq_of, pos_of, rows, seqs, heads, head, capacity, single_wave(blocks, 8));
 }
 
 extern "C" tempo_status tempo_argmax_finish(const float* part_val, const int32_t* part_idx, uint32_t rows,

@@ -46,6 +46,7 @@ struct RowMajorParams {
   uint32_t ldo, ldr;
   uint32_t flags;
   uint32_t m_tiles, n_tiles;
+  uint32_t stages;  // split-K: shared-memory ring depth actually used (<= the template's STAGES)
   KvStore kv;  // QKV projection: key and value columns also stored into the caches
 };
 
@@ -58,13 +59,20 @@ struct RowMajorSmem {
   // full[S], empty[S], acc_full[2], acc_empty[2], final
   static constexpr uint32_t kBarriers = 2 * STAGES + 5;
   static constexpr uint32_t kExchangeOffset = kBarrierOffset + kBarriers * 8 + 16;  // after tmem slot and abort flag
-  // argmax mode: the upper column half's best value and index per tile row, handed to the lower half
+  // argmax mode: one column group's best value and index per tile row, handed to the next lower group
   static constexpr uint32_t kBytes = kExchangeOffset + 128 * 8 + 1024;  // + alignment slack
+  // At most 195 KB: the 196 KB carveout, leaving L1 to the kernels that overlap this one on the SM.
+  static_assert(kBytes <= 195 * 1024, "row-major GEMM shared memory exceeds the 196 KB carveout");
 };
 
-// Warp roles of the row-major kernel: 0 TMA, 1 MMA, 2..9 epilogue. Epilogue warp w reads TMEM lane quarter w % 4
-// (the quarter a warp may access) and column half (w - 2) / 4 of each tile, so two warps share every row.
-constexpr int kRowThreads = 320;
+// Warp roles of the row-major kernel: 0 TMA, 1 MMA, 2..17 epilogue. Epilogue warp w reads TMEM lane quarter w % 4
+// (the quarter a warp may access) and column quarter (w - 2) / 4 of each tile, so four warps share every row and
+// the bias / GELU / store work of a 128 x BN tile is spread over 512 threads.
+constexpr uint32_t kRowEpiGroups = 4;
+constexpr int kRowEpiThreads = 128 * kRowEpiGroups;
+constexpr int kRowThreads = 64 + kRowEpiThreads;
+// The split-K kernel keeps 0 TMA, 1 MMA, 2..9 epilogue (two CTAs may share an SM).
+constexpr int kSplitThreads = 320;
 constexpr int kEpilogueThreads = 256;
 
 template <int BN, int STAGES>
@@ -96,7 +104,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], kEpilogueThreads);
+      mbar_init(&acc_empty[a], kRowEpiThreads);
     }
     mbar_init(final_bar, 1);
     *abort_flag = 0;
@@ -175,11 +183,12 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       mbar_wait(final_bar, 0, kWatchOther, nullptr);
     }
   } else {
-    // Epilogue: warp owns TMEM lanes 32*(warp%4) .. +31 (tile rows) and one half of the tile's columns.
+    // Epilogue: warp owns TMEM lanes 32*(warp%4) .. +31 (tile rows) and one quarter of the tile's columns.
     const uint32_t lane_base = 32u * (warp & 3u);
     const uint32_t row_in_tile = lane_base + lane;
-    const uint32_t half = (warp - 2) >> 2;
-    constexpr uint32_t kHalf = BN / 2;
+    const uint32_t group = (warp - 2) >> 2;
+    constexpr uint32_t kGroupCols = BN / kRowEpiGroups;
+    constexpr uint32_t kCW = kGroupCols >= 32 ? 32 : 16;  // columns per TMEM load
     float* exchange_val = reinterpret_cast<float*>(smem + L::kExchangeOffset);
     int32_t* exchange_idx = reinterpret_cast<int32_t*>(exchange_val + 128);
     uint32_t acc = 0, acc_phase = 0;
@@ -194,29 +203,33 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       float best = -INFINITY;
       int32_t best_idx = 0;
 #pragma unroll 1
-      for (uint32_t c = half * kHalf; c < (half + 1) * kHalf; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + acc * BN + c, r);
+      for (uint32_t c = group * kGroupCols; c < (group + 1) * kGroupCols; c += kCW) {
+        uint32_t r[kCW];
+        if constexpr (kCW == 32) {
+          tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + acc * BN + c, r);
+        } else {
+          tmem_ld_32x32b_x16(tmem_base + (lane_base << 16) + acc * BN + c, r);
+        }
         tmem_wait_ld();
         const uint32_t n0 = n_blk * BN + c;
         if (!row_ok || n0 >= p.n) continue;
         if (argmax) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
+          for (uint32_t j = 0; j < kCW; ++j) {
             const float v = __uint_as_float(r[j]);
             if (n0 + j < p.n && v > best) { best = v; best_idx = int32_t(n0 + j); }
           }
           continue;
         }
-        float v[32];
+        float v[kCW];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        const bool full_chunk = n0 + 32 <= p.n;
+        for (uint32_t j = 0; j < kCW; ++j) v[j] = __uint_as_float(r[j]);
+        const bool full_chunk = n0 + kCW <= p.n;
         if (p.bias != nullptr) {
           if (full_chunk) {
             const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (uint32_t q = 0; q < kCW / 8; ++q) {
               const uint4 w = __ldg(b4 + q);
               const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -226,13 +239,13 @@ __global__ void __launch_bounds__(kRowThreads, 1)
               }
             }
           } else {
-            for (int j = 0; j < 32; ++j)
+            for (uint32_t j = 0; j < kCW; ++j)
               if (n0 + j < p.n) v[j] += bf16_to_float(p.bias[n0 + j]);
           }
         }
         if (gelu) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = gelu_erf(round_bf16(v[j]));
+          for (uint32_t j = 0; j < kCW; ++j) v[j] = gelu_erf(round_bf16(v[j]));
         }
         uint16_t* orow = p.out + size_t(row) * p.ldo;
         if (p.residual != nullptr) {
@@ -240,7 +253,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
           if (full_chunk) {
             const uint4* r4 = reinterpret_cast<const uint4*>(rrow + n0);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (uint32_t q = 0; q < kCW / 8; ++q) {
               const uint4 w = r4[q];
               const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -250,7 +263,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
               }
             }
           } else {
-            for (int j = 0; j < 32; ++j)
+            for (uint32_t j = 0; j < kCW; ++j)
               if (n0 + j < p.n) v[j] += bf16_to_float(rrow[n0 + j]);
           }
         }
@@ -258,7 +271,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
           uint4* o4 = reinterpret_cast<uint4*>(orow + n0);
           uint4* cache4 = reinterpret_cast<uint4*>(kv_destination(p.kv, row, n0));
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (uint32_t q = 0; q < kCW / 8; ++q) {
             uint4 w;
             w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
             w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
@@ -268,25 +281,32 @@ __global__ void __launch_bounds__(kRowThreads, 1)
             if (cache4 != nullptr) cache4[q] = w;
           }
         } else {
-          for (int j = 0; j < 32; ++j)
+          for (uint32_t j = 0; j < kCW; ++j)
             if (n0 + j < p.n) orow[n0 + j] = float_to_bf16(v[j]);
         }
       }
       if (argmax) {
-        // The upper half hands its best to the lower half, which keeps the earlier index on a tie.
-        const uint32_t pair_barrier = 1 + (warp & 3u);
-        if (half == 1) {
-          exchange_val[row_in_tile] = best;
-          exchange_idx[row_in_tile] = best_idx;
+        // The best of each row passes down the column groups, highest first, each keeping its own (earlier) index
+        // on a tie; group 0 writes the tile's partial. One 128-row slot (1 KB) carries it.
+        const uint32_t quarter_barrier = 1 + (warp & 3u);
+#pragma unroll 1
+        for (uint32_t g = kRowEpiGroups - 1; g >= 1; --g) {
+          if (group == g) {
+            exchange_val[row_in_tile] = best;
+            exchange_idx[row_in_tile] = best_idx;
+          }
+          asm volatile("bar.sync %0, %1;" ::"r"(quarter_barrier), "r"(32 * kRowEpiGroups) : "memory");
+          if (group == g - 1) {
+            const float other = exchange_val[row_in_tile];
+            if (other > best) { best = other; best_idx = exchange_idx[row_in_tile]; }
+          }
         }
-        asm volatile("bar.sync %0, 64;" ::"r"(pair_barrier) : "memory");
-        if (half == 0 && row_ok) {
-          const float other = exchange_val[row_in_tile];
-          if (other > best) { best = other; best_idx = exchange_idx[row_in_tile]; }
+        if (group == 0 && row_ok) {
           p.part_val[size_t(row) * p.n_tiles + n_blk] = best;
           p.part_idx[size_t(row) * p.n_tiles + n_blk] = best_idx;
         }
-        asm volatile("bar.sync %0, 64;" ::"r"(pair_barrier) : "memory");
+        // The slot is free again only once group 0 has read it.
+        asm volatile("bar.sync %0, %1;" ::"r"(quarter_barrier), "r"(32 * kRowEpiGroups) : "memory");
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
@@ -498,8 +518,11 @@ tempo_status launch_rowmajor(const void* a, uint32_t lda, const void* w_t, uint3
 // Split-K for small M (the decode projections): a cluster of SPLITS CTAs shares one 128 x BN output tile, each CTA
 // running a contiguous share of the k-blocks into its own TMEM accumulator. The FP32 partial tiles are reduced
 // through distributed shared memory: CTA r owns rows [r*128/SPLITS, (r+1)*128/SPLITS) of the tile, every CTA writes
-// its partial rows into the owner's shared memory, one cluster barrier, and each owner sums its rows and runs the
-// epilogue with coalesced 16-byte stores. No workspace and no atomics.
+// its partial rows (those inside M) into the owner's shared memory, one cluster barrier, and each owner sums its rows
+// and runs the epilogue with coalesced 16-byte stores. No workspace and no atomics. The 16-byte chunks of partial row
+// r are XOR-swizzled by r % 8, so the 32 lanes of a warp, one row each, store into different banks without padding
+// (the shared memory stays within the 196 KB carveout, which leaves 60 KB of L1 to kernels sharing the SM). The ring
+// holds only as many stages as a split has k-blocks.
 // ---------------------------------------------------------------------------------------------------------------
 
 template <int BN, int SPLITS, int STAGES>
@@ -508,11 +531,15 @@ struct SplitSmem {
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kRowsPer = 128 / SPLITS;
-  static constexpr uint32_t kRedOffset = STAGES * kStageBytes;
-  static constexpr uint32_t kRedBytes = 128 * BN * 4;  // [SPLITS][kRowsPer][BN] FP32 partials of the owned rows
-  static constexpr uint32_t kBarrierOffset = kRedOffset + kRedBytes;
+  static constexpr uint32_t kRedBytes = 128 * BN * 4;  // [SPLITS][kRowsPer][BN] FP32 partials, chunks swizzled
   static constexpr uint32_t kBarriers = 2 * STAGES + 2;  // full, empty, acc_full, final
-  static constexpr uint32_t kBytes = kBarrierOffset + kBarriers * 8 + 16 + 1024;
+  __host__ __device__ static constexpr uint32_t red_offset(uint32_t stages) { return stages * kStageBytes; }
+  __host__ __device__ static constexpr uint32_t barrier_offset(uint32_t stages) { return red_offset(stages) + kRedBytes; }
+  __host__ __device__ static constexpr uint32_t bytes(uint32_t stages) {
+    return barrier_offset(stages) + kBarriers * 8 + 16 + 1024;
+  }
+  static_assert(barrier_offset(STAGES) + kBarriers * 8 + 16 + 1024 <= 195 * 1024,
+                "split-K GEMM shared memory exceeds the 196 KB carveout");
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -537,14 +564,15 @@ __device__ __forceinline__ void cluster_sync_all() {
 }
 
 template <int BN, int SPLITS, int STAGES>
-__global__ void __launch_bounds__(kRowThreads, 1)
+__global__ void __launch_bounds__(kSplitThreads, 1)
     gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                        RowMajorParams p) {
   using L = SplitSmem<BN, SPLITS, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* red = reinterpret_cast<float*>(smem + L::kRedOffset);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarrierOffset);
+  const uint32_t stages = p.stages;
+  float* red = reinterpret_cast<float*>(smem + L::red_offset(stages));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::barrier_offset(stages));
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* acc_full = bars + 2 * STAGES;
@@ -590,7 +618,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       bool used[STAGES];
       for (int s = 0; s < STAGES; ++s) used[s] = false;
       // The weights do not depend on the previous kernel: the first ring's worth streams in before the wait.
-      const uint32_t early = (kb1 - kb0) < uint32_t(STAGES) ? (kb1 - kb0) : uint32_t(STAGES);
+      const uint32_t early = (kb1 - kb0) < stages ? (kb1 - kb0) : stages;
       for (uint32_t i = 0; i < early; ++i) {
         mbar_arrive_expect_tx(&full[i], L::kStageBytes);
         tma_load_2d(smem + i * L::kStageBytes + L::kABytes, &tmap_b, &full[i], int32_t((kb0 + i) * kBK),
@@ -609,7 +637,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
         tma_load_2d(a_dst, &tmap_a, &full[stage], int32_t(kb * kBK), int32_t(m_blk * 128));
         used[stage] = true;
         last_parity[stage] = phase;
-        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        if (++stage == stages) { stage = 0; phase ^= 1u; }
       }
       for (int s = 0; s < STAGES; ++s)
         if (used[s]) mbar_wait(&full[s], last_parity[s], kWatchFull, nullptr);
@@ -631,7 +659,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
           umma_bf16(tmem_base, a_desc, b_desc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
         }
         umma_commit(&empty[stage]);
-        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        if (++stage == stages) { stage = 0; phase ^= 1u; }
       }
       if (ok) umma_commit(acc_full);
       umma_commit(final_bar);
@@ -647,16 +675,20 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     if (have_acc) {
       tc_fence_after();
       const uint32_t owner = row_in_tile / L::kRowsPer, owned_row = row_in_tile % L::kRowsPer;
-      const uint32_t local = smem_u32(red + (size_t(rank) * L::kRowsPer + owned_row) * BN);
-      const uint32_t remote = map_to_rank(local, owner);
+      const uint32_t slot = rank * L::kRowsPer + owned_row;
+      const uint32_t remote = map_to_rank(smem_u32(red + size_t(slot) * BN), owner);
+      const bool inside = m_blk * 128 + row_in_tile < p.m;
 #pragma unroll 1
       for (uint32_t c = half * kHalf; c < (half + 1) * kHalf; c += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + c, r);
         tmem_wait_ld();
+        if (inside) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) st_cluster_v4(remote + (c + q * 4) * 4, r[q * 4], r[q * 4 + 1], r[q * 4 + 2],
-                                                   r[q * 4 + 3]);
+          for (uint32_t q = 0; q < 8; ++q)
+            st_cluster_v4(remote + (((c / 4 + q) ^ (slot & 7u)) * 16), r[q * 4], r[q * 4 + 1], r[q * 4 + 2],
+                          r[q * 4 + 3]);
+        }
       }
     }
   }
@@ -678,9 +710,10 @@ __global__ void __launch_bounds__(kRowThreads, 1)
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[j] = 0.f;
 #pragma unroll
-      for (int s = 0; s < SPLITS; ++s) {
-        const float4* src = reinterpret_cast<const float4*>(red + (size_t(s) * L::kRowsPer + lr) * BN + c8 * 8);
-        const float4 x = src[0], y = src[1];
+      for (uint32_t s = 0; s < uint32_t(SPLITS); ++s) {
+        const uint32_t slot = s * L::kRowsPer + lr;
+        const float4* row_base = reinterpret_cast<const float4*>(red + size_t(slot) * BN);
+        const float4 x = row_base[(2 * c8) ^ (slot & 7u)], y = row_base[(2 * c8 + 1) ^ (slot & 7u)];
         v[0] += x.x; v[1] += x.y; v[2] += x.z; v[3] += x.w;
         v[4] += y.x; v[5] += y.y; v[6] += y.z; v[7] += y.w;
       }
@@ -744,10 +777,12 @@ tempo_status launch_splitk(const void* a, uint32_t lda, const void* w_t, uint32_
   RowMajorParams p = base;
   p.m_tiles = (p.m + 127) / 128;
   p.n_tiles = (p.n + BN - 1) / BN;
+  const uint32_t per_split = ((p.k + kBK - 1) / kBK + SPLITS - 1) / SPLITS;
+  p.stages = per_split < uint32_t(STAGES) ? per_split : uint32_t(STAGES);
   auto kernel = gemm_splitk_kernel<BN, SPLITS, STAGES>;
-  s = set_smem(reinterpret_cast<const void*>(kernel), L::kBytes);
+  s = set_smem(reinterpret_cast<const void*>(kernel), L::bytes(STAGES));
   if (s != TEMPO_OK) return s;
-  return launch(kernel, dim3(p.m_tiles * p.n_tiles * SPLITS), dim3(kRowThreads), L::kBytes, stream, SPLITS,
+  return launch(kernel, dim3(p.m_tiles * p.n_tiles * SPLITS), dim3(kSplitThreads), L::bytes(p.stages), stream, SPLITS,
                 "gemm_splitk_kernel", ta, tb, p);
 }
 

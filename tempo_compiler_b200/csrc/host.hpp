@@ -38,6 +38,11 @@ tempo_status set_smem(const void* kernel, int bytes);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Whether a grid of `ctas` fits on the GPU at once with `per_sm` resident per SM. A kernel whose grid does lets its
+// dependents launch at entry (their prologue overlaps the whole kernel); one that needs several waves triggers them
+// only after its own work, so their CTAs do not take SM resources its later waves still need.
+inline uint32_t single_wave(uint64_t ctas, uint32_t per_sm) { return ctas <= uint64_t(sm_count()) * per_sm ? 1u : 0u; }
+
 // Launches `kernel` with programmatic stream serialization (it may overlap the tail of the previous kernel in the
 // stream; the kernel itself waits with griddepcontrol.wait before reading anything that kernel wrote) and, when
 // cluster_x > 1, as clusters of cluster_x CTAs along x.

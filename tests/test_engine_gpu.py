@@ -83,6 +83,21 @@ def test_prefill_and_decode_greedy_tokens_match_the_oracle() -> None:
     np.testing.assert_array_equal(eager, tokens)
 
 
+def test_grouped_decode_matches_the_oracle() -> None:
+    """Decode split into three uneven sequence groups on three CUDA streams (1 + 2 + 2 sequences)."""
+    from tempo_compiler_b200.engine import Engine
+    from tempo_compiler_b200.weights import random_gpt2, random_token_ids
+    layers, shared = random_gpt2(33)
+    batch, prompt, steps = 5, 32, 12
+    ids = np.stack([random_token_ids(200 + s, prompt) for s in range(batch)]).astype(np.int32)
+    engine = Engine(layers, shared, batch=batch, prompt=prompt, capacity=prompt + steps, decode_groups=3)
+    assert engine.decode_groups == [(0, 1), (1, 3), (3, 5)]
+    tokens = engine.generate(ids, steps)
+    for s in range(batch):
+        _check_teacher_forced(layers, shared, ids[s], tokens[s])
+    np.testing.assert_array_equal(engine.generate(ids, steps, graph=False), tokens)
+
+
 def test_free_running_greedy_identity_on_a_short_decode() -> None:
     from tempo_compiler_b200.engine import Engine
     from tempo_compiler_b200.weights import random_gpt2, random_token_ids

@@ -350,7 +350,12 @@ def _fused_packed_cache(cache: np.ndarray) -> np.ndarray:
     return np.concatenate([_packed_block(cache[b * 32:(b + 1) * 32]) for b in range(cache.shape[0] // 32)])
 
 
-@pytest.mark.parametrize(("seqs", "capacity", "lengths"), [(3, 64, (1, 33, 64)), (2, 1152, (1024, 1100))])
+@pytest.mark.parametrize(("seqs", "capacity", "lengths"), [
+    (3, 64, (1, 33, 64)),               # one CTA per (sequence, head)
+    (2, 1152, (1024, 1100)),            # eight CTAs per (sequence, head), the last one's key range empty
+    (4, 512, (0, 1, 200, 512)),         # four per pair: empty, single-key and ragged lengths
+    (90, 256, tuple(range(1, 91))),     # two per pair, every length 1..90
+])
 def test_native_decode_attention_matches_fp32(seqs: int, capacity: int, lengths) -> None:
     from tempo_compiler_b200 import ops
     g = torch.Generator(device="cuda").manual_seed(capacity)
@@ -360,6 +365,9 @@ def test_native_decode_attention_matches_fp32(seqs: int, capacity: int, lengths)
     lens = torch.tensor(lengths, dtype=torch.int32, device="cuda")
     out = ops.decode_attention(qkv, kc, vc, lens)
     for s, length in enumerate(lengths):
+        if length == 0:
+            assert not out[s].float().abs().any(), "an empty cache attends to nothing"
+            continue
         q = qkv[s, :768].float().view(12, 1, 64)
         scores = q @ kc[s, :, :length].float().transpose(1, 2)
         ref = (scores.softmax(-1) @ vc[s, :, :length].float()).reshape(768)
