@@ -163,6 +163,7 @@ tempo_status tempo_block_copy(const void* source, void* destination, uint32_t ro
 
 #define TEMPO_GEMM_GELU 1u   /* out = GELU(round_bf16(acc + bias)) */
 #define TEMPO_GEMM_ARGMAX 2u /* no output: per-row (max, first argmax) over each N tile into the partials */
+#define TEMPO_GEMM_LN 4u     /* internal: the LayerNorm-folded mode of tempo_gemm_ln (rejected by tempo_gemm) */
 
 /* out[M, ldo] = epilogue(a[M, K] (row stride lda) x w_t[N, K]^T (row stride ldw)) with optional bias[N] and
  * residual[M, ldr] (added after GELU), FP32 accumulate, BF16 out; tcgen05 + TMA. K % 8 == 0; lda, ldw % 8 == 0.
@@ -181,6 +182,19 @@ tempo_status tempo_gemm_qkv(const void* a, uint32_t lda, const void* w_t, uint32
                             uint32_t ldo, uint32_t m, uint32_t k, void* k_cache, void* v_cache, uint32_t seqs,
                             uint32_t heads, uint32_t head, uint32_t capacity, uint32_t tokens_per_seq,
                             const int32_t* positions, void* stream);
+
+/* A projection with the LayerNorm before it folded in: layernorm_resident followed by gemm_resident
+ * (board_package/gpt2_inference.py:474-503 and :574-640) as one kernel, for the decode step. With wg = gamma x W
+ * (w_t_folded[N, K] is W^T with column k scaled by gamma[k], BF16), colsum[n] = sum_k wg[n, k] (FP32, of the BF16
+ * wg) and bias_folded[n] = b[n] + sum_k beta[k] W[k, n] (FP32):
+ *   out[r, n] = epilogue(rstd_r * (sum_k x[r, k] wg[n, k] - mean_r * colsum[n]) + bias_folded[n]),
+ * mean_r and rstd_r = 1 / sqrt(var_r + epsilon) being row r's statistics, computed in the kernel while its MMAs run.
+ * flags: 0 or TEMPO_GEMM_GELU. With k_cache / v_cache non-NULL the key and value columns are also stored into the
+ * caches as tempo_gemm_qkv stores them in decode (positions required, N == 3 * heads * head). */
+tempo_status tempo_gemm_ln(const void* x, uint32_t ldx, const void* w_t_folded, uint32_t ldw, const float* colsum,
+                           const float* bias_folded, float epsilon, void* out, uint32_t ldo, uint32_t m, uint32_t n,
+                           uint32_t k, uint32_t flags, void* k_cache, void* v_cache, uint32_t seqs, uint32_t heads,
+                           uint32_t head, uint32_t capacity, const int32_t* positions, void* stream);
 
 /* Row-wise LayerNorm of `rows` BF16 rows of `features` (features % 8 == 0, <= 4096) read `x_stride` elements apart
  * (x_stride % 8 == 0), FP32 statistics, BF16 out [rows, features]. */

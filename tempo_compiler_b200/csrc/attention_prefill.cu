@@ -218,19 +218,22 @@ __global__ void __launch_bounds__(kThreads, 2)
       tmem_ld_32x32b_x32(buf + lane_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(sr + 0));
       tmem_ld_32x32b_x32(buf + lane_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
       tmem_wait_ld();
-      float mx = -INFINITY;
       if (j >= first_masked) {
         // Keys past the query, and past the sequence end, are masked.
 #pragma unroll
         for (uint32_t c = 0; c < kKeys; ++c) {
           const uint32_t key = j * kKeys + c;
           if (key > q_local || key >= p.tokens) sr[c] = __float_as_uint(-INFINITY);
-          mx = fmaxf(mx, __uint_as_float(sr[c]));
         }
-      } else {
-#pragma unroll
-        for (uint32_t c = 0; c < kKeys; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
       }
+      // Eight independent partial maxima (short dependency chains), then combined.
+      float mxs[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mxs[i] = __uint_as_float(sr[i]);
+#pragma unroll
+      for (uint32_t c = 8; c < kKeys; ++c) mxs[c % 8] = fmaxf(mxs[c % 8], __uint_as_float(sr[c]));
+      const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
       bool rescale = false;
       float factor = 1.f;
       if (m_used == -INFINITY) {
@@ -242,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         rescale = true;
       }
       const float base = m_used == -INFINITY ? 0.f : m_used * kLog2e;
-      float sum = 0.f;
+      float sums[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
 #pragma unroll
       for (int c16 = 0; c16 < int(kKeys / 32); ++c16) {
         uint32_t packed[16];
@@ -250,12 +253,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int i = 0; i < 16; ++i) {
           const float e0 = fast_exp2(fmaf(__uint_as_float(sr[c16 * 32 + 2 * i]), kLog2e, -base));
           const float e1 = fast_exp2(fmaf(__uint_as_float(sr[c16 * 32 + 2 * i + 1]), kLog2e, -base));
-          sum += e0 + e1;
+          sums[i % 4] += e0 + e1;
           packed[i] = pack_bf16x2(e0, e1);
         }
         tmem_st_32x32b_x16(buf + lane_addr + c16 * 16, packed);
       }
-      l += sum;
+      l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
       // The rescale must wait for the previous P V (the only MMA writing O) to finish.
       const bool warp_rescale = __any_sync(0xFFFFFFFFu, rescale);
       if (warp_rescale) {

@@ -47,6 +47,14 @@ struct RowMajorParams {
   uint32_t flags;
   uint32_t m_tiles, n_tiles;
   uint32_t stages;  // split-K: shared-memory ring depth actually used (<= the template's STAGES)
+  uint32_t stage_tx;  // bytes one stage's TMA loads deliver: the A box rows (64 when M <= 64) plus the B tile
+  // TEMPO_GEMM_LN: the A operand is the raw rows x; the preceding LayerNorm is folded into the weights (gamma x W),
+  // out = rstd (acc - mean colsum[n]) + ln_bias[n] with FP32 colsum / ln_bias, row statistics computed in-kernel.
+  const uint16_t* ln_x;
+  uint32_t ln_ldx;
+  const float* ln_colsum;
+  const float* ln_bias;
+  float ln_eps;
   KvStore kv;  // QKV projection: key and value columns also stored into the caches
 };
 
@@ -56,8 +64,8 @@ struct RowMajorSmem {
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kBarrierOffset = STAGES * kStageBytes;
-  // full[S], empty[S], acc_full[2], acc_empty[2], final
-  static constexpr uint32_t kBarriers = 2 * STAGES + 5;
+  // full[S], empty[S], acc_full[2], acc_empty[2], final, epilogue-wide (row statistics)
+  static constexpr uint32_t kBarriers = 2 * STAGES + 6;
   static constexpr uint32_t kExchangeOffset = kBarrierOffset + kBarriers * 8 + 16;  // after tmem slot and abort flag
   // argmax mode: one column group's best value and index per tile row, handed to the next lower group
   static constexpr uint32_t kBytes = kExchangeOffset + 128 * 8 + 1024;  // + alignment slack
@@ -75,6 +83,68 @@ constexpr int kRowThreads = 64 + kRowEpiThreads;
 constexpr int kSplitThreads = 320;
 constexpr int kEpilogueThreads = 256;
 
+// Mean and 1/sqrt(var + eps) of `rows` rows of x (k elements, k % 8 == 0) into mean[] / rstd[], computed by the
+// `threads` threads t = 0 .. threads-1: a group of 4-32 consecutive lanes per row, each lane folding 8-element chunks
+// into a running (count, mean, M2) exactly (Chan's parallel update), the group merged by shuffles. Centred
+// variance, so large row means cost no accuracy.
+__device__ __forceinline__ void ln_row_stats(const uint16_t* x, uint32_t ldx, uint32_t k, uint32_t rows, float eps,
+                                             float* mean_out, float* rstd_out, uint32_t t, uint32_t threads) {
+  uint32_t tpr = 32;  // lanes per row: as many as cover every row (rows <= threads / 4)
+  while (tpr > 4 && rows * tpr > threads) tpr /= 2;
+  const uint32_t row = t / tpr, part = t % tpr;
+  const uint32_t chunks = k / 8;
+  float n = 0.f, mean = 0.f, m2 = 0.f;
+  if (row < rows) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + size_t(row) * ldx);
+    constexpr uint32_t kBatch = 8;
+    for (uint32_t base = part; base < chunks; base += kBatch * tpr) {
+      uint4 w[kBatch];
+#pragma unroll
+      for (uint32_t i = 0; i < kBatch; ++i) {
+        const uint32_t c = base + i * tpr;
+        w[i] = c < chunks ? __ldg(xr + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (uint32_t i = 0; i < kBatch; ++i) {
+        if (base + i * tpr >= chunks) break;
+        const uint32_t ws[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+        float v[8], cm = 0.f;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          v[2 * h] = bf16_lo(ws[h]);
+          v[2 * h + 1] = bf16_hi(ws[h]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cm += v[j];
+        cm *= 0.125f;
+        float cm2 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cm2 = fmaf(v[j] - cm, v[j] - cm, cm2);
+        const float n_new = n + 8.f, delta = cm - mean;
+        mean = fmaf(delta, 8.f / n_new, mean);
+        m2 += cm2 + delta * delta * (n * 8.f / n_new);
+        n = n_new;
+      }
+    }
+  }
+  for (uint32_t off = tpr / 2; off >= 1; off /= 2) {
+    const float on = __shfl_xor_sync(0xFFFFFFFFu, n, off);
+    const float om = __shfl_xor_sync(0xFFFFFFFFu, mean, off);
+    const float o2 = __shfl_xor_sync(0xFFFFFFFFu, m2, off);
+    const float tot = n + on;
+    if (tot > 0.f) {
+      const float delta = om - mean;
+      mean = fmaf(delta, on / tot, mean);
+      m2 += o2 + delta * delta * (n * on / tot);
+      n = tot;
+    }
+  }
+  if (row < rows && part == 0) {
+    mean_out[row] = mean;
+    rstd_out[row] = rsqrtf(m2 / float(k) + eps);
+  }
+}
+
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kRowThreads, 1)
     gemm_rowmajor_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -88,6 +158,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   uint64_t* acc_full = bars + 2 * STAGES;
   uint64_t* acc_empty = bars + 2 * STAGES + 2;
   uint64_t* final_bar = bars + 2 * STAGES + 4;
+  uint64_t* epi_bar = bars + 2 * STAGES + 5;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kBarriers);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -107,6 +178,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       mbar_init(&acc_empty[a], kRowEpiThreads);
     }
     mbar_init(final_bar, 1);
+    mbar_init(epi_bar, kRowEpiThreads);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmap_a);
@@ -121,8 +193,8 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_launch_dependents();
-  // Everything below reads operands or writes outputs the previous kernel in the stream may still be using.
-  pdl_wait();
+  // The A operand, the residual and the output may belong to the previous kernel in the stream: the producer waits
+  // for it after prefetching weights, the epilogue before its first access. The MMA warp reads only shared memory.
 
   if (warp == 0) {
     if (elect_one()) {
@@ -131,20 +203,36 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       bool used[STAGES];
       for (int s = 0; s < STAGES; ++s) used[s] = false;
       bool ok = true;
+      // The weights are not the previous kernel's output: the first tile's first ring of B tiles streams in before
+      // the wait.
+      const uint32_t early = blockIdx.x < tiles ? (kblocks < uint32_t(STAGES) ? kblocks : uint32_t(STAGES)) : 0u;
+      if (early > 0) {
+        const int32_t n0 = int32_t((blockIdx.x % p.n_tiles) * BN);
+        for (uint32_t kb = 0; kb < early; ++kb) {
+          mbar_arrive_expect_tx(&full[kb], p.stage_tx);
+          tma_load_2d(smem + kb * L::kStageBytes + L::kABytes, &tmap_b, &full[kb], int32_t(kb * kBK), n0);
+          used[kb] = true;  // a copy is in flight on this stage from here on
+          last_parity[kb] = 0;
+        }
+      }
+      pdl_wait();
+      bool first = true;
       for (uint32_t t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         const int32_t m0 = int32_t((t / p.n_tiles) * 128);
         const int32_t n0 = int32_t((t % p.n_tiles) * BN);
         for (uint32_t kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, kWatchEmpty, abort_flag)) { ok = false; break; }
           uint8_t* a_dst = smem + stage * L::kStageBytes;
-          uint8_t* b_dst = a_dst + L::kABytes;
-          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          if (!(first && kb < early)) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, kWatchEmpty, abort_flag)) { ok = false; break; }
+            mbar_arrive_expect_tx(&full[stage], p.stage_tx);
+            tma_load_2d(a_dst + L::kABytes, &tmap_b, &full[stage], int32_t(kb * kBK), n0);
+          }
           tma_load_2d(a_dst, &tmap_a, &full[stage], int32_t(kb * kBK), m0);
-          tma_load_2d(b_dst, &tmap_b, &full[stage], int32_t(kb * kBK), n0);
           used[stage] = true;
           last_parity[stage] = phase;
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
+        first = false;
       }
       // Every copy this thread issued must have landed before the CTA may exit.
       for (int s = 0; s < STAGES; ++s)
@@ -187,14 +275,39 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     const uint32_t lane_base = 32u * (warp & 3u);
     const uint32_t row_in_tile = lane_base + lane;
     const uint32_t group = (warp - 2) >> 2;
-    constexpr uint32_t kGroupCols = BN / kRowEpiGroups;
+    // Narrow tiles (BN 16 or 32) leave the upper column groups idle: every group needs 16 columns or more.
+    constexpr uint32_t kActiveGroups = BN / 16 < kRowEpiGroups ? BN / 16 : kRowEpiGroups;
+    constexpr uint32_t kGroupCols = BN / kActiveGroups;
     constexpr uint32_t kCW = kGroupCols >= 32 ? 32 : 16;  // columns per TMEM load
+    static_assert(kActiveGroups >= 1 && kGroupCols % kCW == 0, "row-major tile width");
     float* exchange_val = reinterpret_cast<float*>(smem + L::kExchangeOffset);
     int32_t* exchange_idx = reinterpret_cast<int32_t*>(exchange_val + 128);
     uint32_t acc = 0, acc_phase = 0;
+    pdl_wait();
+    const bool ln = (p.flags & TEMPO_GEMM_LN) != 0;
+    float* ln_mean = exchange_val;  // the argmax hand-off slot: the two modes are exclusive
+    float* ln_rstd = exchange_val + 128;
+    uint32_t ln_block = 0xFFFFFFFFu, epi_phase = 0;
+    // Every epilogue thread arrives; the wait is bounded, so a thread that left the loop cannot stall the others.
+    auto epi_sync = [&]() -> bool {
+      mbar_arrive(epi_bar);
+      const bool ok = mbar_wait(epi_bar, epi_phase, kWatchOther, abort_flag);
+      epi_phase ^= 1u;
+      return ok;
+    };
     const bool gelu = (p.flags & TEMPO_GEMM_GELU) != 0;
     const bool argmax = (p.flags & TEMPO_GEMM_ARGMAX) != 0;
     for (uint32_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+      if (ln && t / p.n_tiles != ln_block) {
+        // Row statistics of this tile's 128-row block, while its MMAs run (the slots are free once every epilogue
+        // thread is done with the previous block's).
+        ln_block = t / p.n_tiles;
+        if (!epi_sync()) break;
+        const uint32_t rows = p.m - ln_block * 128 < 128u ? p.m - ln_block * 128 : 128u;
+        ln_row_stats(p.ln_x + size_t(ln_block) * 128 * p.ln_ldx, p.ln_ldx, p.k, rows, p.ln_eps, ln_mean, ln_rstd,
+                     threadIdx.x - 64, kRowEpiThreads);
+        if (!epi_sync()) break;
+      }
       if (!mbar_wait(&acc_full[acc], acc_phase, kWatchAccFull, abort_flag)) break;
       tc_fence_after();
       const uint32_t m_blk = t / p.n_tiles, n_blk = t % p.n_tiles;
@@ -203,7 +316,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       float best = -INFINITY;
       int32_t best_idx = 0;
 #pragma unroll 1
-      for (uint32_t c = group * kGroupCols; c < (group + 1) * kGroupCols; c += kCW) {
+      for (uint32_t c = group * kGroupCols; group < kActiveGroups && c < (group + 1) * kGroupCols; c += kCW) {
         uint32_t r[kCW];
         if constexpr (kCW == 32) {
           tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + acc * BN + c, r);
@@ -225,6 +338,14 @@ __global__ void __launch_bounds__(kRowThreads, 1)
 #pragma unroll
         for (uint32_t j = 0; j < kCW; ++j) v[j] = __uint_as_float(r[j]);
         const bool full_chunk = n0 + kCW <= p.n;
+        if (ln) {
+          // LayerNorm folded into the weights: rstd (x (gamma W) - mean colsum) + (beta W + b).
+          const float mu = ln_mean[row_in_tile], rs = ln_rstd[row_in_tile];
+          for (uint32_t j = 0; j < kCW; ++j) {
+            const uint32_t col = n0 + j < p.n ? n0 + j : p.n - 1;
+            v[j] = fmaf(rs, fmaf(-mu, __ldg(p.ln_colsum + col), v[j]), __ldg(p.ln_bias + col));
+          }
+        }
         if (p.bias != nullptr) {
           if (full_chunk) {
             const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0);
@@ -494,7 +615,9 @@ tempo_status launch_rowmajor(const void* a, uint32_t lda, const void* w_t, uint3
   CUtensorMap ta, tb;
   const uint64_t a_dims[2] = {base.k, base.m};
   const uint64_t a_strides[1] = {uint64_t(lda) * 2};
-  const uint32_t a_box[2] = {kBK, 128};
+  // At most 64 rows: a 64-row box, so the copy fills no out-of-range rows (the MMA's upper 64 rows are discarded).
+  const uint32_t a_rows = base.m <= 64 ? 64 : 128;
+  const uint32_t a_box[2] = {kBK, a_rows};
   tempo_status s = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, a_dims, a_strides, a_box,
                                CU_TENSOR_MAP_SWIZZLE_128B);
   if (s != TEMPO_OK) return s;
@@ -504,6 +627,7 @@ tempo_status launch_rowmajor(const void* a, uint32_t lda, const void* w_t, uint3
   s = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_t, b_dims, b_strides, b_box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (s != TEMPO_OK) return s;
   RowMajorParams p = base;
+  p.stage_tx = a_rows * kBK * 2 + L::kBBytes;
   p.m_tiles = (p.m + 127) / 128;
   p.n_tiles = (p.n + BN - 1) / BN;
   const uint32_t tiles = p.m_tiles * p.n_tiles;
@@ -620,7 +744,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       // The weights do not depend on the previous kernel: the first ring's worth streams in before the wait.
       const uint32_t early = (kb1 - kb0) < stages ? (kb1 - kb0) : stages;
       for (uint32_t i = 0; i < early; ++i) {
-        mbar_arrive_expect_tx(&full[i], L::kStageBytes);
+        mbar_arrive_expect_tx(&full[i], p.stage_tx);
         tma_load_2d(smem + i * L::kStageBytes + L::kABytes, &tmap_b, &full[i], int32_t((kb0 + i) * kBK),
                     int32_t(n_blk * BN));
         used[i] = true;  // a copy is in flight on this stage from here on
@@ -631,7 +755,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         uint8_t* a_dst = smem + stage * L::kStageBytes;
         if (kb - kb0 >= early) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, kWatchEmpty, abort_flag)) break;
-          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          mbar_arrive_expect_tx(&full[stage], p.stage_tx);
           tma_load_2d(a_dst + L::kABytes, &tmap_b, &full[stage], int32_t(kb * kBK), int32_t(n_blk * BN));
         }
         tma_load_2d(a_dst, &tmap_a, &full[stage], int32_t(kb * kBK), int32_t(m_blk * 128));
@@ -765,7 +889,9 @@ tempo_status launch_splitk(const void* a, uint32_t lda, const void* w_t, uint32_
   CUtensorMap ta, tb;
   const uint64_t a_dims[2] = {base.k, base.m};
   const uint64_t a_strides[1] = {uint64_t(lda) * 2};
-  const uint32_t a_box[2] = {kBK, 128};
+  // At most 64 rows: a 64-row box, so the copy fills no out-of-range rows (the MMA's upper 64 rows are discarded).
+  const uint32_t a_rows = base.m <= 64 ? 64 : 128;
+  const uint32_t a_box[2] = {kBK, a_rows};
   tempo_status s = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, a_dims, a_strides, a_box,
                                CU_TENSOR_MAP_SWIZZLE_128B);
   if (s != TEMPO_OK) return s;
@@ -775,6 +901,7 @@ tempo_status launch_splitk(const void* a, uint32_t lda, const void* w_t, uint32_
   s = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_t, b_dims, b_strides, b_box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (s != TEMPO_OK) return s;
   RowMajorParams p = base;
+  p.stage_tx = a_rows * kBK * 2 + L::kBBytes;
   p.m_tiles = (p.m + 127) / 128;
   p.n_tiles = (p.n + BN - 1) / BN;
   const uint32_t per_split = ((p.k + kBK - 1) / kBK + SPLITS - 1) / SPLITS;
@@ -786,8 +913,10 @@ tempo_status launch_splitk(const void* a, uint32_t lda, const void* w_t, uint32_
                 "gemm_splitk_kernel", ta, tb, p);
 }
 
-// Picks a split-K configuration for a GEMM whose 128-row tiles alone leave SMs idle: the most CTAs (tiles x splits)
-// that still fit one wave, each split keeping at least two k-blocks. Returns false when the plain kernel is better.
+// Picks a split-K configuration for a GEMM whose 128-row tiles alone leave SMs idle: the most CTAs (tiles x splits,
+// two or more splits) that still fit one wave, each split keeping at least two k-blocks. Returns false when the
+// plain kernel is better (including when only an unsplit grid fits: the persistent kernel runs that without a
+// reduction step).
 bool pick_split(uint32_t m, uint32_t n, uint32_t k, uint32_t* bn, uint32_t* splits) {
   const uint32_t sms = uint32_t(sm_count());
   const uint32_t m_tiles = (m + 127) / 128, kblocks = (k + kBK - 1) / kBK;
@@ -795,7 +924,7 @@ bool pick_split(uint32_t m, uint32_t n, uint32_t k, uint32_t* bn, uint32_t* spli
   uint32_t best_ctas = 0;
   for (uint32_t cand_bn : {128u, 64u}) {
     const uint32_t tiles = m_tiles * ((n + cand_bn - 1) / cand_bn);
-    for (uint32_t s : {1u, 2u, 4u, 8u}) {
+    for (uint32_t s : {2u, 4u, 8u}) {
       const uint64_t ctas = uint64_t(tiles) * s;
       if (ctas > sms || kblocks < 2 * s) continue;
       if (ctas > best_ctas) {
@@ -814,17 +943,26 @@ bool pick_split(uint32_t m, uint32_t n, uint32_t k, uint32_t* bn, uint32_t* spli
 
 using namespace tempo;
 
+// The LayerNorm folded into a projection (TEMPO_GEMM_LN): FP32 column sums of the folded weights, the folded bias
+// and the epsilon.
+struct LnFold {
+  const float* colsum = nullptr;
+  const float* bias = nullptr;
+  float eps = 0.f;
+};
+
 static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
                               const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m, uint32_t n,
                               uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx, const KvStore& kv,
-                              void* stream);
+                              const LnFold& ln, void* stream);
 
 extern "C" tempo_status tempo_gemm(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
                                    const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m,
                                    uint32_t n, uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx,
                                    void* stream) {
+  if (flags & TEMPO_GEMM_LN) return fail(TEMPO_ERR_VALUE, "tempo_gemm: TEMPO_GEMM_LN is tempo_gemm_ln's mode");
   return gemm_impl(a, lda, w_t, ldw, bias, residual, ldr, out, ldo, m, n, k, flags, part_val, part_idx, KvStore{},
-                   stream);
+                   LnFold{}, stream);
 }
 
 extern "C" tempo_status tempo_gemm_qkv(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
@@ -840,19 +978,44 @@ extern "C" tempo_status tempo_gemm_qkv(const void* a, uint32_t lda, const void* 
                 heads, head, seqs, capacity, tokens_per_seq);
   KvStore kv{static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), positions, tokens_per_seq, seqs,
              heads, head, capacity, width};
-  return gemm_impl(a, lda, w_t, ldw, bias, nullptr, 0, out, ldo, m, 3 * width, k, 0, nullptr, nullptr, kv, stream);
+  return gemm_impl(a, lda, w_t, ldw, bias, nullptr, 0, out, ldo, m, 3 * width, k, 0, nullptr, nullptr, kv, LnFold{},
+                   stream);
+}
+
+extern "C" tempo_status tempo_gemm_ln(const void* x, uint32_t ldx, const void* w_t_folded, uint32_t ldw,
+                                      const float* colsum, const float* bias_folded, float epsilon, void* out,
+                                      uint32_t ldo, uint32_t m, uint32_t n, uint32_t k, uint32_t flags, void* k_cache,
+                                      void* v_cache, uint32_t seqs, uint32_t heads, uint32_t head, uint32_t capacity,
+                                      const int32_t* positions, void* stream) {
+  if (colsum == nullptr || bias_folded == nullptr || !aligned16(colsum) || !aligned16(bias_folded))
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm_ln: column sums and folded bias are needed, 16-byte aligned");
+  if (flags & ~TEMPO_GEMM_GELU) return fail(TEMPO_ERR_VALUE, "tempo_gemm_ln: only TEMPO_GEMM_GELU may be set");
+  KvStore kv{};
+  if (k_cache != nullptr || v_cache != nullptr) {
+    const uint32_t width = heads * head;
+    if (k_cache == nullptr || v_cache == nullptr || !aligned16(k_cache) || !aligned16(v_cache) || positions == nullptr)
+      return fail(TEMPO_ERR_VALUE, "tempo_gemm_ln: the cache store needs both caches (16-byte aligned) and positions");
+    if (heads == 0 || head == 0 || head % 32 || seqs == 0 || capacity == 0 || n != 3 * width)
+      return fail(TEMPO_ERR_VALUE, "tempo_gemm_ln: heads %u head %u (multiple of 32) seqs %u capacity %u, N %u", heads,
+                  head, seqs, capacity, n);
+    kv = KvStore{static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), positions, 0, seqs, heads, head,
+                 capacity, width};
+  }
+  return gemm_impl(x, ldx, w_t_folded, ldw, nullptr, nullptr, 0, out, ldo, m, n, k, flags | TEMPO_GEMM_LN, nullptr,
+                   nullptr, kv, LnFold{colsum, bias_folded, epsilon}, stream);
 }
 
 static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
                               const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m, uint32_t n,
                               uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx, const KvStore& kv,
-                              void* stream) {
+                              const LnFold& ln, void* stream) {
   if (m == 0 || n == 0 || k == 0) return fail(TEMPO_ERR_VALUE, "tempo_gemm: empty problem %ux%ux%u", m, n, k);
   if (k % 8 || lda % 8 || ldw % 8 || lda < k || ldw < k)
     return fail(TEMPO_ERR_VALUE, "tempo_gemm: K (%u) and the row strides (%u, %u) must be multiples of 8 and >= K", k,
                 lda, ldw);
   if (!aligned16(a) || !aligned16(w_t)) return fail(TEMPO_ERR_VALUE, "tempo_gemm: operands must be 16-byte aligned");
   const bool argmax = (flags & TEMPO_GEMM_ARGMAX) != 0;
+  if (argmax && (flags & TEMPO_GEMM_LN)) return fail(TEMPO_ERR_VALUE, "tempo_gemm: argmax with a folded LayerNorm");
   if (argmax && (part_val == nullptr || part_idx == nullptr))
     return fail(TEMPO_ERR_VALUE, "tempo_gemm: argmax mode needs the partial buffers");
   if (!argmax && (out == nullptr || ldo < n || (ldo % 8) || !aligned16(out)))
@@ -873,27 +1036,41 @@ static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint
   p.ldr = ldr;
   p.flags = flags;
   p.kv = kv;
+  const bool ln_mode = (flags & TEMPO_GEMM_LN) != 0;
+  if (ln_mode) {
+    p.ln_x = static_cast<const uint16_t*>(a);
+    p.ln_ldx = lda;
+    p.ln_colsum = ln.colsum;
+    p.ln_bias = ln.bias;
+    p.ln_eps = ln.eps;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // A handful of rows (decode of a few sequences): stream the weights on the CUDA cores instead.
-  if (m <= 8) {
+  if (m <= 8 && !ln_mode) {
     const tempo_status gemv = gemv_dispatch(a, lda, w_t, ldw, bias, residual, ldr, out, ldo, m, n, k, flags, part_val,
                                             part_idx, kv, st);
     if (gemv != TEMPO_ERR_VALUE) return gemv;
   }
   if (argmax) return launch_rowmajor<256, 4>(a, lda, w_t, ldw, p, st);
+  // One 128-row block with a short contraction (the decode projections of up to 128 sequences): narrow tiles over the
+  // whole of K, at most one per SM, need no cross-CTA reduction.
+  if (m <= 128 && k <= 1024) {
+    const uint32_t sms = uint32_t(sm_count());
+    if ((n + 15) / 16 <= sms) return launch_rowmajor<16, 8>(a, lda, w_t, ldw, p, st);
+    if ((n + 31) / 32 <= sms) return launch_rowmajor<32, 8>(a, lda, w_t, ldw, p, st);
+  }
   // Small M (decode): split the contraction over a cluster so every SM has work.
   uint32_t bn = 0, splits = 0;
-  if (n % 8 == 0 && pick_split(m, n, k, &bn, &splits)) {
+  // The folded LayerNorm needs every k of a row in one CTA: no split-K.
+  if (!ln_mode && n % 8 == 0 && pick_split(m, n, k, &bn, &splits)) {
     if (bn == 128) {
       switch (splits) {
-        case 1: return launch_splitk<128, 1, 4>(a, lda, w_t, ldw, p, st);
         case 2: return launch_splitk<128, 2, 4>(a, lda, w_t, ldw, p, st);
         case 4: return launch_splitk<128, 4, 4>(a, lda, w_t, ldw, p, st);
         default: return launch_splitk<128, 8, 4>(a, lda, w_t, ldw, p, st);
       }
     }
     switch (splits) {
-      case 1: return launch_splitk<64, 1, 6>(a, lda, w_t, ldw, p, st);
       case 2: return launch_splitk<64, 2, 6>(a, lda, w_t, ldw, p, st);
       case 4: return launch_splitk<64, 4, 6>(a, lda, w_t, ldw, p, st);
       default: return launch_splitk<64, 8, 6>(a, lda, w_t, ldw, p, st);

@@ -38,6 +38,20 @@ def _bf16(array: np.ndarray, device) -> torch.Tensor:
     return torch.from_numpy(np.ascontiguousarray(array, dtype=np.float32)).to(device).to(torch.bfloat16)
 
 
+def fold_layernorm(gamma: torch.Tensor, beta: torch.Tensor, w_t: torch.Tensor, bias: torch.Tensor | None
+                   ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """The operands of gemm_ln for LayerNorm(gamma, beta) followed by x @ W + bias (w_t = W^T, [N, K] BF16): the folded
+    BF16 weights (gamma scaling W's rows), their FP32 column sums and the FP32 folded bias b + beta @ W. Computed once
+    per weight set, in float64 on the device (weight preparation, not the decode path)."""
+    w64 = w_t.double()
+    folded = (w64 * gamma.double()[None, :]).to(torch.bfloat16).contiguous()
+    colsum = folded.double().sum(dim=1).float().contiguous()
+    b = w64 @ beta.double()
+    if bias is not None:
+        b = b + bias.double()
+    return folded, colsum, b.float().contiguous()
+
+
 @dataclass
 class LayerWeights:
     ln1_g: torch.Tensor
@@ -52,6 +66,9 @@ class LayerWeights:
     b_fc: torch.Tensor
     w_out: torch.Tensor   # [W, 4W]
     b_out: torch.Tensor
+    # decode with the LayerNorms folded into the QKV and FC projections (fold_layernorm's operands)
+    qkv_folded: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None
+    fc_folded: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None
 
 
 class Engine:
@@ -63,6 +80,9 @@ class Engine:
         prompt: tokens per prompt (every sequence of a batch has the same length).
         capacity: cache positions per sequence (prompt + decode steps).
         device: the CUDA device.
+        fold_layernorms: decode folds each block's two LayerNorms into the QKV and FC projections
+            (``ops.gemm_ln``), so a layer runs five kernels instead of seven (default: on above 8 sequences; 8 or
+            fewer rows take the CUDA-core GEMV path, which has no folded form).
         decode_groups: the decode step splits the batch into this many groups of sequences, each on its own CUDA
             stream (default 1). The groups are independent, so one group's bandwidth-bound attention may overlap
             another's projections; on a B200 the extra, smaller launches cost more than the overlap gains (512
@@ -71,7 +91,7 @@ class Engine:
 
     def __init__(self, layers: list[dict], shared: dict, *, batch: int, prompt: int, capacity: int,
                  shape: GPT2Shape = GPT2_SMALL, device: str | torch.device = "cuda",
-                 decode_groups: int | None = None) -> None:
+                 decode_groups: int | None = None, fold_layernorms: bool | None = None) -> None:
         if not torch.cuda.is_available():
             raise RuntimeError("the B200 engine needs a CUDA device; there is no CPU path")
         self.device = torch.device(device)
@@ -95,6 +115,11 @@ class Engine:
         self.wpe = _bf16(shared["wpe"], self.device)
         self.lnf_g = _bf16(shared["ln_f.g"], self.device)
         self.lnf_b = _bf16(shared["ln_f.b"], self.device)
+        self.fold_layernorms = batch > 8 if fold_layernorms is None else fold_layernorms
+        if self.fold_layernorms:
+            for lw in self.layers:
+                lw.qkv_folded = fold_layernorm(lw.ln1_g, lw.ln1_b, lw.w_qkv, lw.b_qkv)
+                lw.fc_folded = fold_layernorm(lw.ln2_g, lw.ln2_b, lw.w_fc, lw.b_fc)
         n_layers = len(layers)
         cache_shape = (batch, heads, capacity, shape.head)
         self.k_cache = [torch.empty(cache_shape, dtype=torch.bfloat16, device=self.device) for _ in range(n_layers)]
@@ -137,6 +162,9 @@ class Engine:
 
     def _layer(self, lw: LayerWeights, index: int, x, ln, qkv, attn, h, *, decode: bool,
                seqs: slice = slice(None)) -> None:
+        if decode and self.fold_layernorms:
+            self._folded_decode_layer(lw, index, x, qkv, attn, h, seqs)
+            return
         ops.layernorm(x, lw.ln1_g, lw.ln1_b, epsilon=LN_EPSILON, out=ln)
         # the projection's epilogue also writes this step's keys and values into the layer's cache
         k_cache, v_cache = self.k_cache[index][seqs], self.v_cache[index][seqs]
@@ -150,6 +178,18 @@ class Engine:
         ops.gemm(attn, lw.w_proj, bias=lw.b_proj, residual=x, out=x)
         ops.layernorm(x, lw.ln2_g, lw.ln2_b, epsilon=LN_EPSILON, out=ln)
         ops.gemm(ln, lw.w_fc, bias=lw.b_fc, gelu=True, out=h)
+        ops.gemm(h, lw.w_out, bias=lw.b_out, residual=x, out=x)
+
+    def _folded_decode_layer(self, lw: LayerWeights, index: int, x, qkv, attn, h, seqs: slice) -> None:
+        """One decode block with both LayerNorms folded into the projections after them."""
+        k_cache, v_cache = self.k_cache[index][seqs], self.v_cache[index][seqs]
+        positions = self.positions[seqs]
+        w, cs, bf = lw.qkv_folded
+        ops.gemm_ln(x, w, cs, bf, epsilon=LN_EPSILON, out=qkv, k_cache=k_cache, v_cache=v_cache, positions=positions)
+        ops.decode_attention(qkv, k_cache, v_cache, positions, length_offset=1, out=attn)
+        ops.gemm(attn, lw.w_proj, bias=lw.b_proj, residual=x, out=x)
+        w, cs, bf = lw.fc_folded
+        ops.gemm_ln(x, w, cs, bf, epsilon=LN_EPSILON, gelu=True, out=h)
         ops.gemm(h, lw.w_out, bias=lw.b_out, residual=x, out=x)
 
     def prefill(self, token_ids: torch.Tensor) -> None:

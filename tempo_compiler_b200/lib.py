@@ -23,6 +23,7 @@ IMAGE_MAGIC = 0x49324254
 IMAGE_BYTES = 64
 GEMM_GELU = 1
 GEMM_ARGMAX = 2
+GEMM_LN = 4
 
 _EXCEPTIONS = {ERR_VALUE: ValueError, ERR_MEMORY: MemoryError, ERR_KEY: KeyError, ERR_RUNTIME: RuntimeError,
                ERR_TIMEOUT: TimeoutError, ERR_STATE: RuntimeError}
@@ -58,6 +59,8 @@ _SIGNATURES = {
     "tempo_gemm": [_vp, _u32, _vp, _u32, _vp, _vp, _u32, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp, _vp],
     "tempo_gemm_qkv": [_vp, _u32, _vp, _u32, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp,
                        _vp],
+    "tempo_gemm_ln": [_vp, _u32, _vp, _u32, _vp, _vp, _f32, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp, _u32, _u32,
+                      _u32, _u32, _vp, _vp],
     "tempo_layernorm": [_vp, _u32, _vp, _vp, _vp, _u32, _u32, _f32, _vp],
     "tempo_embed": [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp],
     "tempo_attention_prefill": [_vp, _vp, _u32, _u32, _u32, _u32, _vp],

@@ -84,6 +84,33 @@ def gemm_qkv(a: torch.Tensor, w_t: torch.Tensor, bias: torch.Tensor, out: torch.
     return out
 
 
+def gemm_ln(x: torch.Tensor, w_folded: torch.Tensor, colsum: torch.Tensor, bias_folded: torch.Tensor, *,
+            epsilon: float = 1e-5, gelu: bool = False, out: torch.Tensor | None = None,
+            k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None,
+            positions: torch.Tensor | None = None) -> torch.Tensor:
+    """out = epilogue(LayerNorm(x) @ W + b) with the LayerNorm folded into the weights: w_folded[N, K] = (gamma * W)^T
+    in BF16, colsum[N] = its FP32 row sums, bias_folded[N] = b + beta @ W in FP32; the row statistics are computed in
+    the kernel. With the caches (and positions) the key and value columns are also stored, as in gemm_qkv decode."""
+    _check(x, torch.bfloat16, "x")
+    _check(w_folded, torch.bfloat16, "w_folded")
+    _check(colsum, torch.float32, "colsum")
+    _check(bias_folded, torch.float32, "bias_folded")
+    m, k = x.shape
+    n = w_folded.shape[0]
+    if w_folded.shape[1] != k:
+        raise ValueError(f"inner dimensions differ: x {tuple(x.shape)}, w_folded {tuple(w_folded.shape)}")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    _check(out, torch.bfloat16, "out")
+    seqs = heads = head = capacity = 0
+    if k_cache is not None:
+        seqs, heads, capacity, head = k_cache.shape
+    _launch("tempo_gemm_ln", x.data_ptr(), k, w_folded.data_ptr(), k, colsum.data_ptr(), bias_folded.data_ptr(),
+            float(epsilon), out.data_ptr(), out.shape[1], m, n, k, _lib.GEMM_GELU if gelu else 0, _ptr(k_cache),
+            _ptr(v_cache), seqs, heads, head, capacity, _ptr(positions), _stream())
+    return out
+
+
 def gemm_argmax(a: torch.Tensor, w_t: torch.Tensor, part_val: torch.Tensor, part_idx: torch.Tensor) -> None:
     """Per-row (max, first argmax) of a @ w_t^T over each 256-column tile into the partial buffers [M, ceil(N/256)]."""
     _check(a, torch.bfloat16, "a")

@@ -257,6 +257,56 @@ def test_gemm_qkv_writes_keys_and_values_into_the_cache(seqs: int, tokens: int, 
     assert torch.equal(vc, expected_v)
 
 
+@pytest.mark.parametrize(("m", "n", "gelu"), [(3, 2304, False), (64, 2304, False), (64, 3072, True),
+                                               (128, 3072, True), (200, 2304, False), (512, 3072, True)])
+def test_gemm_ln_matches_layernorm_then_gemm(m: int, n: int, gelu: bool) -> None:
+    """LayerNorm folded into the projection: against torch fp32 LayerNorm -> BF16 -> matmul (+ bias, GELU), with
+    non-trivial gamma / beta and rows whose mean is far from zero (the in-kernel statistics are centred)."""
+    from tempo_compiler_b200 import ops
+    from tempo_compiler_b200.engine import fold_layernorm
+    g = torch.Generator(device="cuda").manual_seed(m + n)
+    x = (torch.randn((m, 768), generator=g, device="cuda") * 3.0
+         + torch.randn((m, 1), generator=g, device="cuda") * 40.0).to(torch.bfloat16)
+    gamma = (1.0 + 0.2 * torch.randn(768, generator=g, device="cuda")).to(torch.bfloat16)
+    beta = (0.1 * torch.randn(768, generator=g, device="cuda")).to(torch.bfloat16)
+    w = (torch.randn((n, 768), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    folded, colsum, bias_folded = fold_layernorm(gamma, beta, w, bias)
+    out = ops.gemm_ln(x, folded, colsum, bias_folded, epsilon=1e-5, gelu=gelu)
+    ln = torch.nn.functional.layer_norm(x.float(), (768,), gamma.float(), beta.float(), 1e-5).to(torch.bfloat16)
+    ref = ln.float() @ w.float().T + bias.float()
+    if gelu:
+        ref = torch.nn.functional.gelu(ref.to(torch.bfloat16).float())
+    error = ((out.float() - ref).norm() / ref.norm()).item()
+    assert error < 1e-2, error
+    assert ops.watchdog() == 0
+
+
+def test_gemm_ln_stores_keys_and_values() -> None:
+    """The folded QKV projection with the decode cache store: the caches receive exactly its key and value columns."""
+    from tempo_compiler_b200 import ops
+    from tempo_compiler_b200.engine import fold_layernorm
+    g = torch.Generator(device="cuda").manual_seed(77)
+    seqs, capacity = 40, 20
+    x = torch.randn((seqs, 768), generator=g, device="cuda").to(torch.bfloat16)
+    gamma = (1.0 + 0.1 * torch.randn(768, generator=g, device="cuda")).to(torch.bfloat16)
+    beta = (0.1 * torch.randn(768, generator=g, device="cuda")).to(torch.bfloat16)
+    w = (torch.randn((2304, 768), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    folded, colsum, bias_folded = fold_layernorm(gamma, beta, w, None)
+    kc = torch.full((seqs, 12, capacity, 64), 7.0, dtype=torch.bfloat16, device="cuda")
+    vc = torch.full_like(kc, 7.0)
+    positions = torch.randint(0, capacity + 3, (seqs,), generator=g, device="cuda", dtype=torch.int32)
+    out = ops.gemm_ln(x, folded, colsum, bias_folded, k_cache=kc, v_cache=vc, positions=positions)
+    expected_k, expected_v = torch.full_like(kc, 7.0), torch.full_like(vc, 7.0)
+    for r in range(seqs):
+        p = int(positions[r])
+        if p < capacity:
+            expected_k[r, :, p] = out[r, 768:1536].view(12, 64)
+            expected_v[r, :, p] = out[r, 1536:].view(12, 64)
+    assert torch.equal(kc, expected_k)
+    assert torch.equal(vc, expected_v)
+
+
 def test_gemm_argmax_matches_torch() -> None:
     from tempo_compiler_b200 import ops
     g = torch.Generator(device="cuda").manual_seed(5)
