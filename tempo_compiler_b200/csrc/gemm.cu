@@ -145,6 +145,84 @@ __device__ __forceinline__ void ln_row_stats(const uint16_t* x, uint32_t ldx, ui
   }
 }
 
+// One thread's kCW accumulator columns n0 .. n0 + kCW - 1 of output row `row`: the folded LayerNorm (mean / rstd of the
+// row), bias, exact-erf GELU of the BF16-rounded sum, residual, BF16 stores into the output and, for the QKV
+// projection, into the key / value caches.
+template <uint32_t kCW>
+__device__ __forceinline__ void epilogue_chunk(const RowMajorParams& p, const uint32_t (&r)[kCW], uint32_t row,
+                                               uint32_t n0, bool gelu, bool ln, float mu, float rs) {
+  float v[kCW];
+#pragma unroll
+  for (uint32_t j = 0; j < kCW; ++j) v[j] = __uint_as_float(r[j]);
+  const bool full_chunk = n0 + kCW <= p.n;
+  if (ln) {
+    // LayerNorm folded into the weights: rstd (x (gamma W) - mean colsum) + (beta W + b).
+    for (uint32_t j = 0; j < kCW; ++j) {
+      const uint32_t col = n0 + j < p.n ? n0 + j : p.n - 1;
+      v[j] = fmaf(rs, fmaf(-mu, __ldg(p.ln_colsum + col), v[j]), __ldg(p.ln_bias + col));
+    }
+  }
+  if (p.bias != nullptr) {
+    if (full_chunk) {
+      const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0);
+#pragma unroll
+      for (uint32_t q = 0; q < kCW / 8; ++q) {
+        const uint4 w = __ldg(b4 + q);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          v[q * 8 + 2 * h] += bf16_lo(ws[h]);
+          v[q * 8 + 2 * h + 1] += bf16_hi(ws[h]);
+        }
+      }
+    } else {
+      for (uint32_t j = 0; j < kCW; ++j)
+        if (n0 + j < p.n) v[j] += bf16_to_float(p.bias[n0 + j]);
+    }
+  }
+  if (gelu) {
+#pragma unroll
+    for (uint32_t j = 0; j < kCW; ++j) v[j] = gelu_erf(round_bf16(v[j]));
+  }
+  uint16_t* orow = p.out + size_t(row) * p.ldo;
+  if (p.residual != nullptr) {
+    const uint16_t* rrow = p.residual + size_t(row) * p.ldr;
+    if (full_chunk) {
+      const uint4* r4 = reinterpret_cast<const uint4*>(rrow + n0);
+#pragma unroll
+      for (uint32_t q = 0; q < kCW / 8; ++q) {
+        const uint4 w = r4[q];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          v[q * 8 + 2 * h] += bf16_lo(ws[h]);
+          v[q * 8 + 2 * h + 1] += bf16_hi(ws[h]);
+        }
+      }
+    } else {
+      for (uint32_t j = 0; j < kCW; ++j)
+        if (n0 + j < p.n) v[j] += bf16_to_float(rrow[n0 + j]);
+    }
+  }
+  if (full_chunk) {
+    uint4* o4 = reinterpret_cast<uint4*>(orow + n0);
+    uint4* cache4 = reinterpret_cast<uint4*>(kv_destination(p.kv, row, n0));
+#pragma unroll
+    for (uint32_t q = 0; q < kCW / 8; ++q) {
+      uint4 w;
+      w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+      w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+      w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+      w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+      o4[q] = w;
+      if (cache4 != nullptr) cache4[q] = w;
+    }
+  } else {
+    for (uint32_t j = 0; j < kCW; ++j)
+      if (n0 + j < p.n) orow[n0 + j] = float_to_bf16(v[j]);
+  }
+}
+
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kRowThreads, 1)
     gemm_rowmajor_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -334,77 +412,8 @@ __global__ void __launch_bounds__(kRowThreads, 1)
           }
           continue;
         }
-        float v[kCW];
-#pragma unroll
-        for (uint32_t j = 0; j < kCW; ++j) v[j] = __uint_as_float(r[j]);
-        const bool full_chunk = n0 + kCW <= p.n;
-        if (ln) {
-          // LayerNorm folded into the weights: rstd (x (gamma W) - mean colsum) + (beta W + b).
-          const float mu = ln_mean[row_in_tile], rs = ln_rstd[row_in_tile];
-          for (uint32_t j = 0; j < kCW; ++j) {
-            const uint32_t col = n0 + j < p.n ? n0 + j : p.n - 1;
-            v[j] = fmaf(rs, fmaf(-mu, __ldg(p.ln_colsum + col), v[j]), __ldg(p.ln_bias + col));
-          }
-        }
-        if (p.bias != nullptr) {
-          if (full_chunk) {
-            const uint4* b4 = reinterpret_cast<const uint4*>(p.bias + n0);
-#pragma unroll
-            for (uint32_t q = 0; q < kCW / 8; ++q) {
-              const uint4 w = __ldg(b4 + q);
-              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                v[q * 8 + 2 * h] += bf16_lo(ws[h]);
-                v[q * 8 + 2 * h + 1] += bf16_hi(ws[h]);
-              }
-            }
-          } else {
-            for (uint32_t j = 0; j < kCW; ++j)
-              if (n0 + j < p.n) v[j] += bf16_to_float(p.bias[n0 + j]);
-          }
-        }
-        if (gelu) {
-#pragma unroll
-          for (uint32_t j = 0; j < kCW; ++j) v[j] = gelu_erf(round_bf16(v[j]));
-        }
-        uint16_t* orow = p.out + size_t(row) * p.ldo;
-        if (p.residual != nullptr) {
-          const uint16_t* rrow = p.residual + size_t(row) * p.ldr;
-          if (full_chunk) {
-            const uint4* r4 = reinterpret_cast<const uint4*>(rrow + n0);
-#pragma unroll
-            for (uint32_t q = 0; q < kCW / 8; ++q) {
-              const uint4 w = r4[q];
-              const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                v[q * 8 + 2 * h] += bf16_lo(ws[h]);
-                v[q * 8 + 2 * h + 1] += bf16_hi(ws[h]);
-              }
-            }
-          } else {
-            for (uint32_t j = 0; j < kCW; ++j)
-              if (n0 + j < p.n) v[j] += bf16_to_float(rrow[n0 + j]);
-          }
-        }
-        if (full_chunk) {
-          uint4* o4 = reinterpret_cast<uint4*>(orow + n0);
-          uint4* cache4 = reinterpret_cast<uint4*>(kv_destination(p.kv, row, n0));
-#pragma unroll
-          for (uint32_t q = 0; q < kCW / 8; ++q) {
-            uint4 w;
-            w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-            w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-            w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-            w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-            o4[q] = w;
-            if (cache4 != nullptr) cache4[q] = w;
-          }
-        } else {
-          for (uint32_t j = 0; j < kCW; ++j)
-            if (n0 + j < p.n) orow[n0 + j] = float_to_bf16(v[j]);
-        }
+        const float mu = ln ? ln_mean[row_in_tile] : 0.f, rs = ln ? ln_rstd[row_in_tile] : 0.f;
+        epilogue_chunk<kCW>(p, r, row, n0, gelu, ln, mu, rs);
       }
       if (argmax) {
         // The best of each row passes down the column groups, highest first, each keeping its own (earlier) index
@@ -913,6 +922,281 @@ tempo_status launch_splitk(const void* a, uint32_t lda, const void* w_t, uint32_
                 "gemm_splitk_kernel", ta, tb, p);
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// CTA-pair GEMM for large M (the prefill projections): a cluster of two CTAs on two SMs computes 256 x 256 output
+// tiles with tcgen05.mma.cta_group::2 (M = 256): CTA r of the pair stages rows [128 r, 128 r + 128) of the A tile
+// and rows [128 r, 128 r + 128) of the tile's 256 weight rows, the leader's MMA reads both CTAs' shared memory, and
+// each CTA's TMEM receives its own 128 output rows x 256 columns. Per SM and k-block that is 32 KB of operands for
+// 128 x 256 x 64 MACs instead of 48 KB, which is what feeds the tensor cores from L2 at this size.
+//   warp 0      TMA (both CTAs; .cta_group::2 copies complete on the leader's full barrier)
+//   warp 1      the leader's MMA issuer; both CTAs' warp 1 allocate and free the pair's TMEM
+//   warps 2-17  epilogue (both CTAs), each warp releasing the accumulator on the leader's barrier
+// No copy uses multicast: every CTA loads its own halves, and the leader signals the peer's barriers with
+// separate (non-multicast) commits addressed to the peer.
+// ---------------------------------------------------------------------------------------------------------------
+
+constexpr uint32_t kPairBN = 256;
+
+template <int STAGES>
+struct PairSmem {
+  static constexpr uint32_t kABytes = 128 * kBK * 2;
+  static constexpr uint32_t kBBytes = 128 * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kBarrierOffset = STAGES * kStageBytes;
+  // full[S] (the leader's), empty[S], acc_full[2], acc_empty[2] (the leader's), final
+  static constexpr uint32_t kBarriers = 2 * STAGES + 5;
+  static constexpr uint32_t kBytes = kBarrierOffset + kBarriers * 8 + 16 + 1024;
+  static_assert(kBytes <= 195 * 1024, "pair GEMM shared memory exceeds the 196 KB carveout");
+};
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t columns) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(columns)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t base, uint32_t columns) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(columns) : "memory");
+}
+
+// D[tmem of both CTAs] (+)= A[both CTAs' smem] x B[both CTAs' smem]^T, issued by the leader.
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  const uint32_t zero = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(zero));
+}
+
+// Arrives on one mbarrier (this CTA's or the peer's, by shared::cluster address) when the pair MMAs this thread issued
+// complete.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+
+// A 2-D tile into this CTA's shared memory, its bytes counted on the leader's barrier (shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster, int32_t c0,
+                                                 int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+template <int STAGES>
+__global__ void __launch_bounds__(kRowThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                     RowMajorParams p) {
+  using L = PairSmem<STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarrierOffset);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;
+  uint64_t* final_bar = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kBarriers);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  constexpr uint32_t kTmemCols = 2 * kPairBN;  // two 256-column accumulators
+  constexpr uint32_t kEpiWarps = kRowEpiThreads / 32;
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const uint32_t pairs = gridDim.x / 2, pair = blockIdx.x / 2;
+  const uint32_t tiles = p.m_tiles * p.n_tiles;  // 256 x 256 tiles
+  const uint32_t kblocks = (p.k + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * kEpiWarps);  // one arrival per epilogue warp of either CTA
+    }
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // Both CTAs' barriers are initialised and the pair's TMEM allocated before either signals the other.
+  cluster_sync_all();
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (elect_one()) {
+      const uint32_t full_leader = map_to_rank(smem_u32(full), 0);
+      uint32_t stage = 0, phase = 0;
+      uint32_t last_parity[STAGES];
+      bool used[STAGES];
+      for (int s = 0; s < STAGES; ++s) used[s] = false;
+      bool ok = true;
+      pdl_wait();
+      for (uint32_t t = pair; t < tiles && ok; t += pairs) {
+        const int32_t m0 = int32_t((t / p.n_tiles) * 256 + rank * 128);
+        const int32_t n0 = int32_t((t % p.n_tiles) * kPairBN + rank * 128);
+        for (uint32_t kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, kWatchEmpty, abort_flag)) { ok = false; break; }
+          uint8_t* a_dst = smem + stage * L::kStageBytes;
+          // The leader expects both CTAs' bytes on its barrier.
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
+          const uint32_t bar = full_leader + stage * 8;
+          tma_load_2d_pair(a_dst, &tmap_a, bar, int32_t(kb * kBK), m0);
+          tma_load_2d_pair(a_dst + L::kABytes, &tmap_b, bar, int32_t(kb * kBK), n0);
+          used[stage] = true;
+          last_parity[stage] = phase;
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // The copies complete on the leader's barrier; a stage's last use is over once the MMA released it here.
+      for (int s = 0; s < STAGES; ++s)
+        if (used[s]) mbar_wait(&empty[s], last_parity[s], kWatchEmpty, nullptr);
+    }
+  } else if (warp == 1) {
+    if (leader && elect_one()) {
+      constexpr uint32_t idesc = make_idesc_bf16(256, kPairBN, 0, 0);
+      const uint32_t peer_empty = map_to_rank(smem_u32(empty), 1);
+      const uint32_t peer_acc_full = map_to_rank(smem_u32(acc_full), 1);
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (uint32_t t = pair; t < tiles && ok; t += pairs) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, kWatchAccEmpty, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kPairBN;
+        for (uint32_t kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, kWatchFull, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+          for (uint32_t kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t a_desc = make_smem_desc(a_addr + kk * 32, 16, 1024, kLayoutSw128);
+            const uint64_t b_desc = make_smem_desc(b_addr + kk * 32, 16, 1024, kLayoutSw128);
+            umma_bf16_pair(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0u);
+          }
+          umma_commit_pair(smem_u32(&empty[stage]));
+          umma_commit_pair(peer_empty + stage * 8);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&acc_full[acc]));
+        umma_commit_pair(peer_acc_full + acc * 8);
+        acc ^= 1u;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // Drain every MMA this thread issued before the pair's TMEM is freed.
+      umma_commit_pair(smem_u32(final_bar));
+      mbar_wait(final_bar, 0, kWatchOther, nullptr);
+    }
+  } else {
+    // Epilogue: this CTA's 128 rows of each 256 x 256 tile, sixteen warps as in the row-major kernel.
+    const uint32_t lane_base = 32u * (warp & 3u);
+    const uint32_t row_in_tile = lane_base + lane;
+    const uint32_t group = (warp - 2) >> 2;
+    constexpr uint32_t kGroupCols = kPairBN / kRowEpiGroups;
+    constexpr uint32_t kCW = 32;
+    const uint32_t acc_empty_leader = map_to_rank(smem_u32(acc_empty), 0);
+    const bool gelu = (p.flags & TEMPO_GEMM_GELU) != 0;
+    uint32_t acc = 0, acc_phase = 0;
+    pdl_wait();
+    for (uint32_t t = pair; t < tiles; t += pairs) {
+      if (!mbar_wait(&acc_full[acc], acc_phase, kWatchAccFull, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t row = (t / p.n_tiles) * 256 + rank * 128 + row_in_tile;
+      const uint32_t n_base = (t % p.n_tiles) * kPairBN;
+#pragma unroll 1
+      for (uint32_t c = group * kGroupCols; c < (group + 1) * kGroupCols; c += kCW) {
+        uint32_t r[kCW];
+        tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + acc * kPairBN + c, r);
+        tmem_wait_ld();
+        const uint32_t n0 = n_base + c;
+        if (row >= p.m || n0 >= p.n) continue;
+        epilogue_chunk<kCW>(p, r, row, n0, gelu, false, 0.f, 0.f);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_leader + acc * 8);
+      acc ^= 1u;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  // Both CTAs are done with the pair's TMEM and shared memory before either frees or leaves.
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+template <int STAGES>
+tempo_status launch_pair(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const RowMajorParams& base,
+                         cudaStream_t stream) {
+  using L = PairSmem<STAGES>;
+  CUtensorMap ta, tb;
+  const uint64_t a_dims[2] = {base.k, base.m};
+  const uint64_t a_strides[1] = {uint64_t(lda) * 2};
+  const uint32_t a_box[2] = {kBK, 128};
+  tempo_status s = encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a, a_dims, a_strides, a_box,
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != TEMPO_OK) return s;
+  const uint64_t b_dims[2] = {base.k, base.n};
+  const uint64_t b_strides[1] = {uint64_t(ldw) * 2};
+  const uint32_t b_box[2] = {kBK, 128};
+  s = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_t, b_dims, b_strides, b_box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != TEMPO_OK) return s;
+  RowMajorParams p = base;
+  p.m_tiles = (p.m + 255) / 256;
+  p.n_tiles = (p.n + kPairBN - 1) / kPairBN;
+  const uint32_t tiles = p.m_tiles * p.n_tiles;
+  auto kernel = gemm_pair_kernel<STAGES>;
+  s = set_smem(reinterpret_cast<const void*>(kernel), L::kBytes);
+  if (s != TEMPO_OK) return s;
+  // The tiles are dealt out statically, so every pair must be resident at once: as many pairs as the GPCs can hold.
+  static int resident_pairs = 0;
+  if (resident_pairs == 0) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(uint32_t(sm_count()) & ~1u);
+    config.blockDim = dim3(kRowThreads);
+    config.dynamicSmemBytes = L::kBytes;
+    cudaLaunchAttribute attribute;
+    attribute.id = cudaLaunchAttributeClusterDimension;
+    attribute.val.clusterDim.x = 2;
+    attribute.val.clusterDim.y = 1;
+    attribute.val.clusterDim.z = 1;
+    config.attrs = &attribute;
+    config.numAttrs = 1;
+    int clusters = 0;
+    const cudaError_t err = cudaOccupancyMaxActiveClusters(&clusters, kernel, &config);
+    if (err != cudaSuccess || clusters <= 0) return cuda_fail(err, "cudaOccupancyMaxActiveClusters(gemm_pair_kernel)");
+    resident_pairs = clusters;
+  }
+  const uint32_t pairs = tiles < uint32_t(resident_pairs) ? tiles : uint32_t(resident_pairs);
+  return launch(kernel, dim3(2 * pairs), dim3(kRowThreads), L::kBytes, stream, 2, "gemm_pair_kernel", ta, tb, p);
+}
+
 // Picks a split-K configuration for a GEMM whose 128-row tiles alone leave SMs idle: the most CTAs (tiles x splits,
 // two or more splits) that still fit one wave, each split keeping at least two k-blocks. Returns false when the
 // plain kernel is better (including when only an unsplit grid fits: the persistent kernel runs that without a
@@ -1076,6 +1360,9 @@ static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint
       default: return launch_splitk<64, 8, 6>(a, lda, w_t, ldw, p, st);
     }
   }
+  // Large problems (prefill): 256 x 256 tiles on CTA pairs, when there are at least four tiles per pair.
+  if (!ln_mode && !argmax && uint64_t((m + 255) / 256) * ((n + 255) / 256) >= 4ull * (uint64_t(sm_count()) / 2))
+    return launch_pair<6>(a, lda, w_t, ldw, p, st);
   // Wide tiles when the grid still fills the GPU; narrower ones otherwise.
   const uint64_t tiles256 = uint64_t((m + 127) / 128) * ((n + 255) / 256);
   if (tiles256 >= uint64_t(sm_count())) return launch_rowmajor<256, 4>(a, lda, w_t, ldw, p, st);

@@ -257,6 +257,48 @@ def test_gemm_qkv_writes_keys_and_values_into_the_cache(seqs: int, tokens: int, 
     assert torch.equal(vc, expected_v)
 
 
+@pytest.mark.parametrize(("m", "n", "k", "epilogue"), [(20000, 3072, 768, "gelu"), (20000, 2304, 768, "bias"),
+                                                      (25700, 768, 3072, "residual"), (19000, 3000, 768, "plain")])
+def test_pair_gemm_matches_fp32_reference(m: int, n: int, k: int, epilogue: str) -> None:
+    """Prefill-sized products (256 x 256 tiles on CTA pairs), ragged M and N included."""
+    from tempo_compiler_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    a = torch.randn((m, k), generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn((n, k), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(n, generator=g, device="cuda") * 0.1).to(torch.bfloat16) if epilogue != "plain" else None
+    residual = torch.randn((m, n), generator=g, device="cuda").to(torch.bfloat16) if epilogue == "residual" else None
+    out = ops.gemm(a, w, bias=bias, residual=residual, gelu=epilogue == "gelu")
+    ref = a.float() @ w.float().T
+    if bias is not None:
+        ref += bias.float()
+    if epilogue == "gelu":
+        ref = torch.nn.functional.gelu(ref.to(torch.bfloat16).float())
+    if residual is not None:
+        ref += residual.float()
+    error = ((out.float() - ref).norm() / ref.norm()).item()
+    assert error < 5e-3, error
+    assert torch.isfinite(out).all()
+    assert ops.watchdog() == 0
+
+
+def test_pair_gemm_qkv_prefill_cache_store() -> None:
+    """The prefill QKV projection of 20 x 1024 tokens on CTA pairs stores every key and value into the caches."""
+    from tempo_compiler_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(11)
+    seqs, tokens = 20, 1024
+    a = torch.randn((seqs * tokens, 768), generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn((2304, 768), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(2304, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    kc = torch.zeros((seqs, 12, tokens, 64), dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    out = torch.empty((seqs * tokens, 2304), dtype=torch.bfloat16, device="cuda")
+    ops.gemm_qkv(a, w, bias, out, kc, vc, tokens_per_seq=tokens)
+    ref = a.float() @ w.float().T + bias.float()
+    assert ((out.float() - ref).norm() / ref.norm()).item() < 5e-3
+    assert torch.equal(kc, out[:, 768:1536].reshape(seqs, tokens, 12, 64).transpose(1, 2))
+    assert torch.equal(vc, out[:, 1536:].reshape(seqs, tokens, 12, 64).transpose(1, 2))
+
+
 @pytest.mark.parametrize(("m", "n", "gelu"), [(3, 2304, False), (64, 2304, False), (64, 3072, True),
                                                (128, 3072, True), (200, 2304, False), (512, 3072, True)])
 def test_gemm_ln_matches_layernorm_then_gemm(m: int, n: int, gelu: bool) -> None:
