@@ -103,8 +103,6 @@ __device__ __forceinline__ float group_dot(const float (&q)[8], const uint4& k) 
 // softmax states on the CTA; with chunks > 1 every CTA then stores its (max, sum, 64 weighted values) into the
 // cluster leader's shared memory, and the leader merges them and writes the output. Few sequences therefore still
 // put every SM to work, with no workspace and no second kernel.
-constexpr int kDecodeKeys = 8;                       // keys per lane group per iteration
-constexpr int kDecodeWarpKeys = 4 * kDecodeKeys;     // keys per warp per iteration
 constexpr uint32_t kDecodeMaxChunks = 8;
 
 __device__ __forceinline__ uint32_t decode_cluster_rank() {
@@ -113,6 +111,9 @@ __device__ __forceinline__ uint32_t decode_cluster_rank() {
   return r;
 }
 
+// KI keys per lane group per iteration (a warp covers 4 KI keys): 8 keeps 16 loads per lane in flight for grids of
+// many waves; 4 halves the registers (about 64) so a grid of up to eight CTAs per SM is resident at once.
+template <int KI>
 __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* __restrict__ qkv,
                                                                const uint16_t* __restrict__ k_cache,
                                                                const uint16_t* __restrict__ v_cache,
@@ -141,10 +142,10 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* _
   st.l = 0.f;
 #pragma unroll
   for (int d = 0; d < 8; ++d) st.acc[d] = 0.f;
-  for (int32_t base = k_begin + int32_t(warp) * kDecodeWarpKeys; base < k_end; base += 4 * kDecodeWarpKeys) {
-    uint4 kk[kDecodeKeys], vv[kDecodeKeys];
+  for (int32_t base = k_begin + int32_t(warp) * 4 * KI; base < k_end; base += 16 * KI) {
+    uint4 kk[KI], vv[KI];
 #pragma unroll
-    for (int i = 0; i < kDecodeKeys; ++i) {
+    for (int i = 0; i < KI; ++i) {
       const int32_t key = base + i * 4 + int32_t(g);
       if (key < k_end) {
         kk[i] = ld_stream(kb4 + size_t(key) * 8 + li);
@@ -154,13 +155,13 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* _
         vv[i] = make_uint4(0, 0, 0, 0);
       }
     }
-    float sc[kDecodeKeys];
+    float sc[KI];
 #pragma unroll
-    for (int i = 0; i < kDecodeKeys; ++i) {
+    for (int i = 0; i < KI; ++i) {
       const float v = group_dot(q, kk[i]);
       sc[i] = (base + i * 4 + int32_t(g) < k_end) ? v : -INFINITY;
     }
-    fold<kDecodeKeys>(st, sc, vv);
+    fold<KI>(st, sc, vv);
   }
   // A grid of several waves lets the next kernel start its prologue only now: a trigger at entry would let that
   // kernel's CTAs take SM resources while later waves of this grid still wait to be scheduled.
@@ -305,8 +306,12 @@ extern "C" tempo_status tempo_decode_attention(const void* qkv, const void* k_ca
   const uint64_t pairs = uint64_t(seqs) * heads, target = uint64_t(sm_count());
   uint32_t chunks = 1;
   while (chunks < kDecodeMaxChunks && pairs * chunks < target && capacity >= 2 * 128 * chunks) chunks *= 2;
-  return launch(decode_attention_kernel, dim3(chunks, heads, seqs), dim3(128), 0, static_cast<cudaStream_t>(stream),
-                chunks, "decode_attention_kernel", static_cast<const uint16_t*>(qkv),
-                static_cast<const uint16_t*>(k_cache), static_cast<const uint16_t*>(v_cache), lengths, length_offset,
-                static_cast<uint16_t*>(out), heads, capacity, single_wave(pairs * chunks, 4));
+  // A grid that fits at eight CTAs per SM runs the 4-key variant, entirely resident; larger grids the 8-key one.
+  const uint64_t ctas = pairs * chunks;
+  const bool small = single_wave(ctas, 8) != 0;
+  auto kernel = small ? decode_attention_kernel<4> : decode_attention_kernel<8>;
+  return launch(kernel, dim3(chunks, heads, seqs), dim3(128), 0, static_cast<cudaStream_t>(stream), chunks,
+                "decode_attention_kernel", static_cast<const uint16_t*>(qkv), static_cast<const uint16_t*>(k_cache),
+                static_cast<const uint16_t*>(v_cache), lengths, length_offset, static_cast<uint16_t*>(out), heads,
+                capacity, small ? 1u : single_wave(ctas, 4));
 }
