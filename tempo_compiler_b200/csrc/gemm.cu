@@ -148,9 +148,18 @@ __device__ __forceinline__ void ln_row_stats(const uint16_t* x, uint32_t ldx, ui
 // One thread's kCW accumulator columns n0 .. n0 + kCW - 1 of output row `row`: the folded LayerNorm (mean / rstd of the
 // row), bias, exact-erf GELU of the BF16-rounded sum, residual, BF16 stores into the output and, for the QKV
 // projection, into the key / value caches.
-template <uint32_t kCW>
+// With kStaged the BF16 row segment goes into `stage_row` (16-byte words XOR-swizzled by `swizzle`) for a TMA store
+// the caller issues; the key / value cache store stays direct.
+template <uint32_t kCW, bool kStaged = false>
 __device__ __forceinline__ void epilogue_chunk(const RowMajorParams& p, const uint32_t (&r)[kCW], uint32_t row,
-                                               uint32_t n0, bool gelu, bool ln, float mu, float rs) {
+                                               uint32_t n0, bool gelu, bool ln, float mu, float rs,
+                                               uint8_t* stage_row = nullptr, uint32_t swizzle = 0) {
+  if (kStaged && row >= p.m) {
+    // A row past M in a staged block: the copy clips it; read nothing for it.
+#pragma unroll
+    for (uint32_t q = 0; q < kCW / 8; ++q) reinterpret_cast<uint4*>(stage_row)[q ^ swizzle] = make_uint4(0, 0, 0, 0);
+    return;
+  }
   float v[kCW];
 #pragma unroll
   for (uint32_t j = 0; j < kCW; ++j) v[j] = __uint_as_float(r[j]);
@@ -204,7 +213,19 @@ __device__ __forceinline__ void epilogue_chunk(const RowMajorParams& p, const ui
         if (n0 + j < p.n) v[j] += bf16_to_float(rrow[n0 + j]);
     }
   }
-  if (full_chunk) {
+  if (kStaged) {
+    uint4* cache4 = full_chunk ? reinterpret_cast<uint4*>(kv_destination(p.kv, row, n0)) : nullptr;
+#pragma unroll
+    for (uint32_t q = 0; q < kCW / 8; ++q) {
+      uint4 w;
+      w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+      w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+      w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+      w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+      reinterpret_cast<uint4*>(stage_row)[q ^ swizzle] = w;
+      if (cache4 != nullptr) cache4[q] = w;
+    }
+  } else if (full_chunk) {
     uint4* o4 = reinterpret_cast<uint4*>(orow + n0);
     uint4* cache4 = reinterpret_cast<uint4*>(kv_destination(p.kv, row, n0));
 #pragma unroll
@@ -942,7 +963,10 @@ struct PairSmem {
   static constexpr uint32_t kABytes = 128 * kBK * 2;
   static constexpr uint32_t kBBytes = 128 * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr uint32_t kBarrierOffset = STAGES * kStageBytes;
+  // One 32 x 32 BF16 staging tile (2 KB) per epilogue warp for the output's TMA stores.
+  static constexpr uint32_t kStagingOffset = STAGES * kStageBytes;
+  static constexpr uint32_t kStagingBytes = (kRowEpiThreads / 32) * 2048;
+  static constexpr uint32_t kBarrierOffset = kStagingOffset + kStagingBytes;
   // full[S] (the leader's), empty[S], acc_full[2], acc_empty[2] (the leader's), final
   static constexpr uint32_t kBarriers = 2 * STAGES + 5;
   static constexpr uint32_t kBytes = kBarrierOffset + kBarriers * 8 + 16 + 1024;
@@ -988,6 +1012,13 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+// A 2-D tile from this CTA's shared memory to global memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
@@ -995,7 +1026,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
 template <int STAGES>
 __global__ void __launch_bounds__(kRowThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                     RowMajorParams p) {
+                     const __grid_constant__ CUtensorMap tmap_out, RowMajorParams p) {
   using L = PairSmem<STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1031,6 +1062,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    tma_prefetch_desc(&tmap_out);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -1118,12 +1150,18 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     constexpr uint32_t kCW = 32;
     const uint32_t acc_empty_leader = map_to_rank(smem_u32(acc_empty), 0);
     const bool gelu = (p.flags & TEMPO_GEMM_GELU) != 0;
+    // This warp's 32 x 32 staging tile: row `lane` at 64 bytes, its four 16-byte words swizzled by (lane / 2) % 4
+    // (the TMA 64-byte swizzle, which also spreads the warp's writes over all banks).
+    uint8_t* staging = smem + L::kStagingOffset + (warp - 2) * 2048;
+    uint8_t* stage_row = staging + lane * 64;
+    const uint32_t swizzle = (lane >> 1) & 3u;
     uint32_t acc = 0, acc_phase = 0;
     pdl_wait();
     for (uint32_t t = pair; t < tiles; t += pairs) {
       if (!mbar_wait(&acc_full[acc], acc_phase, kWatchAccFull, abort_flag)) break;
       tc_fence_after();
-      const uint32_t row = (t / p.n_tiles) * 256 + rank * 128 + row_in_tile;
+      const uint32_t row0 = (t / p.n_tiles) * 256 + rank * 128 + lane_base;  // this warp's first row
+      const uint32_t row = row0 + lane;
       const uint32_t n_base = (t % p.n_tiles) * kPairBN;
 #pragma unroll 1
       for (uint32_t c = group * kGroupCols; c < (group + 1) * kGroupCols; c += kCW) {
@@ -1131,8 +1169,18 @@ __global__ void __launch_bounds__(kRowThreads, 1)
         tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + acc * kPairBN + c, r);
         tmem_wait_ld();
         const uint32_t n0 = n_base + c;
-        if (row >= p.m || n0 >= p.n) continue;
-        epilogue_chunk<kCW>(p, r, row, n0, gelu, false, 0.f, 0.f);
+        if (row0 >= p.m || n0 >= p.n) continue;  // warp-uniform: the whole 32 x 32 block lies outside
+        // The staging tile is free once the previous store from it has been read.
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncwarp();
+        epilogue_chunk<kCW, true>(p, r, row, n0, gelu, false, 0.f, 0.f, stage_row, swizzle);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        // Rows past M and columns past N are clipped by the copy.
+        if (lane == 0) {
+          tma_store_2d(&tmap_out, staging, int32_t(n0), int32_t(row0));
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -1142,7 +1190,9 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     }
   }
 
-  // Both CTAs are done with the pair's TMEM and shared memory before either frees or leaves.
+  // Every output store has completed; both CTAs are done with the pair's TMEM and shared memory before either frees
+  // or leaves.
+  if (warp >= 2 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   tc_fence_before();
   cluster_sync_all();
   if (warp == 1) {
@@ -1166,6 +1216,13 @@ tempo_status launch_pair(const void* a, uint32_t lda, const void* w_t, uint32_t 
   const uint64_t b_strides[1] = {uint64_t(ldw) * 2};
   const uint32_t b_box[2] = {kBK, 128};
   s = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_t, b_dims, b_strides, b_box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (s != TEMPO_OK) return s;
+  CUtensorMap to;
+  const uint64_t o_dims[2] = {base.n, base.m};
+  const uint64_t o_strides[1] = {uint64_t(base.ldo) * 2};
+  const uint32_t o_box[2] = {32, 32};
+  s = encode_tmap(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base.out, o_dims, o_strides, o_box,
+                  CU_TENSOR_MAP_SWIZZLE_64B);
   if (s != TEMPO_OK) return s;
   RowMajorParams p = base;
   p.m_tiles = (p.m + 255) / 256;
@@ -1194,7 +1251,7 @@ tempo_status launch_pair(const void* a, uint32_t lda, const void* w_t, uint32_t 
     resident_pairs = clusters;
   }
   const uint32_t pairs = tiles < uint32_t(resident_pairs) ? tiles : uint32_t(resident_pairs);
-  return launch(kernel, dim3(2 * pairs), dim3(kRowThreads), L::kBytes, stream, 2, "gemm_pair_kernel", ta, tb, p);
+  return launch(kernel, dim3(2 * pairs), dim3(kRowThreads), L::kBytes, stream, 2, "gemm_pair_kernel", ta, tb, to, p);
 }
 
 // Picks a split-K configuration for a GEMM whose 128-row tiles alone leave SMs idle: the most CTAs (tiles x splits,
@@ -1362,7 +1419,7 @@ static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint
   }
   // Large problems (prefill): 256 x 256 tiles on CTA pairs, when there are at least four tiles per pair.
   if (!ln_mode && !argmax && uint64_t((m + 255) / 256) * ((n + 255) / 256) >= 4ull * (uint64_t(sm_count()) / 2))
-    return launch_pair<6>(a, lda, w_t, ldw, p, st);
+    return launch_pair<5>(a, lda, w_t, ldw, p, st);
   // Wide tiles when the grid still fills the GPU; narrower ones otherwise.
   const uint64_t tiles256 = uint64_t((m + 127) / 128) * ((n + 255) / 256);
   if (tiles256 >= uint64_t(sm_count())) return launch_rowmajor<256, 4>(a, lda, w_t, ldw, p, st);
