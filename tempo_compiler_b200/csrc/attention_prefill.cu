@@ -34,7 +34,8 @@ namespace {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only when the maximum grows by more than 2^8
 constexpr int kThreads = 192;
-constexpr uint32_t kKeys = 64;                        // keys per K/V tile
+constexpr uint32_t kKeys = 64;                        // keys per K/V tile (32 or 64)
+constexpr int kCtasPerSm = kKeys == 32 ? 4 : 2;         // TMEM: 2 x kKeys (S, P) + 64 (O) columns per CTA
 constexpr uint32_t kStages = 4;                       // K/V ring depth
 constexpr uint32_t kQBytes = 128 * 64 * 2;            // one 128-query x 64-dim BF16 tile
 constexpr uint32_t kKvTileBytes = kKeys * 64 * 2;     // one 64-key x 64-dim BF16 tile
@@ -57,7 +58,7 @@ constexpr uint32_t kBarCount = 1 + 2 * kStages + 2 + 2 + 1 + 1;
 constexpr uint32_t kSmem = kOffBar + kBarCount * 8 + 16 + 1024;
 
 // TMEM columns: S/P buffer 0 | S/P buffer 1 | O.
-constexpr uint32_t kTmemS0 = 0, kTmemS1 = 64, kTmemO = 128, kTmemCols = 256;
+constexpr uint32_t kTmemS0 = 0, kTmemS1 = kKeys, kTmemO = 2 * kKeys, kTmemCols = kKeys == 32 ? 128 : 256;
 
 template <bool PACKED>
 __device__ __forceinline__ void load_tile(void* dst, const CUtensorMap* map, uint64_t* bar, uint32_t feature_tile16,
@@ -84,7 +85,7 @@ __device__ __forceinline__ uint64_t v_desc(uint32_t tile_addr, uint32_t kk) {
 }
 
 template <bool PACKED>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     attention_prefill_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_kv,
                              PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -143,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     else return int32_t(s * p.tokens + qt * 128);
   };
   auto kv_coord = [&](uint32_t j) -> int32_t {
-    if constexpr (PACKED) return int32_t(j * 2);
+    if constexpr (PACKED) return int32_t(j * (kKeys / 32));
     else return int32_t(s * p.tokens + j * kKeys);
   };
 
@@ -215,8 +216,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!mbar_wait(&s_full[j & 1u], (j >> 1) & 1u, kWatchOther, abort_flag)) { ok = false; break; }
       tc_fence_after();
       uint32_t sr[kKeys];
-      tmem_ld_32x32b_x32(buf + lane_addr + 0, *reinterpret_cast<uint32_t(*)[32]>(sr + 0));
-      tmem_ld_32x32b_x32(buf + lane_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+#pragma unroll
+      for (uint32_t c32 = 0; c32 < kKeys / 32; ++c32)
+        tmem_ld_32x32b_x32(buf + lane_addr + c32 * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c32 * 32));
       tmem_wait_ld();
       if (j >= first_masked) {
         // Keys past the query, and past the sequence end, are masked.
@@ -365,7 +367,7 @@ extern "C" tempo_status tempo_block_attention(const void* constants, void* fused
   p.heads = heads;
   p.q_tiles = (tokens + 127) / 128;
   p.block_bytes = block_bytes;
-  p.early = single_wave(uint64_t(p.q_tiles) * heads, 2);
+  p.early = single_wave(uint64_t(p.q_tiles) * heads, kCtasPerSm);
   if ((s = set_smem(reinterpret_cast<const void*>(attention_prefill_kernel<true>), kSmem))) return s;
   return launch(attention_prefill_kernel<true>, dim3(p.q_tiles * heads), dim3(kThreads), kSmem,
                 static_cast<cudaStream_t>(stream), 1, "attention_prefill_kernel<packed>", map_q, map_kv, p);
@@ -397,7 +399,7 @@ extern "C" tempo_status tempo_attention_prefill(const void* qkv, void* out, uint
   p.q_tiles = (tokens + 127) / 128;
   const uint64_t ctas = uint64_t(p.q_tiles) * heads * seqs;
   if (ctas > 0x7FFFFFFFull) return fail(TEMPO_ERR_VALUE, "tempo_attention_prefill: too many tiles");
-  p.early = single_wave(ctas, 2);
+  p.early = single_wave(ctas, kCtasPerSm);
   if ((s = set_smem(reinterpret_cast<const void*>(attention_prefill_kernel<false>), kSmem))) return s;
   return launch(attention_prefill_kernel<false>, dim3(uint32_t(ctas)), dim3(kThreads), kSmem,
                 static_cast<cudaStream_t>(stream), 1, "attention_prefill_kernel<rowmajor>", map_q, map_kv, p);

@@ -58,12 +58,15 @@ struct RowMajorParams {
   KvStore kv;  // QKV projection: key and value columns also stored into the caches
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool STAGED = false>
 struct RowMajorSmem {
   static constexpr uint32_t kABytes = 128 * kBK * 2;
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr uint32_t kBarrierOffset = STAGES * kStageBytes;
+  // STAGED: one 32 x 32 BF16 staging tile (2 KB) per epilogue warp for TMA stores of the output.
+  static constexpr uint32_t kStagingOffset = STAGES * kStageBytes;
+  static constexpr uint32_t kStagingBytes = STAGED ? 16u * 2048u : 0u;
+  static constexpr uint32_t kBarrierOffset = kStagingOffset + kStagingBytes;
   // full[S], empty[S], acc_full[2], acc_empty[2], final, epilogue-wide (row statistics)
   static constexpr uint32_t kBarriers = 2 * STAGES + 6;
   static constexpr uint32_t kExchangeOffset = kBarrierOffset + kBarriers * 8 + 16;  // after tmem slot and abort flag
@@ -143,6 +146,13 @@ __device__ __forceinline__ void ln_row_stats(const uint16_t* x, uint32_t ldx, ui
     mean_out[row] = mean;
     rstd_out[row] = rsqrtf(m2 / float(k) + eps);
   }
+}
+
+// A 2-D tile from this CTA's shared memory to global memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(c0), "r"(c1)
+               : "memory");
 }
 
 // One thread's kCW accumulator columns n0 .. n0 + kCW - 1 of output row `row`: the folded LayerNorm (mean / rstd of the
@@ -244,11 +254,12 @@ __device__ __forceinline__ void epilogue_chunk(const RowMajorParams& p, const ui
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool STAGED>
 __global__ void __launch_bounds__(kRowThreads, 1)
     gemm_rowmajor_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                         RowMajorParams p) {
-  using L = RowMajorSmem<BN, STAGES>;
+                         const __grid_constant__ CUtensorMap tmap_out, RowMajorParams p) {
+  using L = RowMajorSmem<BN, STAGES, STAGED>;
+  static_assert(!STAGED || BN >= 128, "staged stores need 32-column chunks");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarrierOffset);
@@ -282,6 +293,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    if (STAGED) tma_prefetch_desc(&tmap_out);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -424,6 +436,24 @@ __global__ void __launch_bounds__(kRowThreads, 1)
         }
         tmem_wait_ld();
         const uint32_t n0 = n_blk * BN + c;
+        if constexpr (STAGED) {
+          // The warp's 32 x 32 block through its staging tile and one TMA store (rows past M and columns past N are
+          // clipped by the copy). Never in argmax mode.
+          const uint32_t row0 = m_blk * 128 + lane_base;
+          if (row0 >= p.m || n0 >= p.n) continue;  // warp-uniform
+          uint8_t* staging = smem + L::kStagingOffset + (warp - 2) * 2048;
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          __syncwarp();
+          const float mu = ln ? ln_mean[row_in_tile] : 0.f, rs = ln ? ln_rstd[row_in_tile] : 0.f;
+          epilogue_chunk<kCW, true>(p, r, row, n0, gelu, ln, mu, rs, staging + lane * 64, (lane >> 1) & 3u);
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_out, staging, int32_t(n0), int32_t(row0));
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+          continue;
+        }
         if (!row_ok || n0 >= p.n) continue;
         if (argmax) {
 #pragma unroll
@@ -466,6 +496,7 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     }
   }
 
+  if (STAGED && warp >= 2 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -638,10 +669,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool STAGED = false>
 tempo_status launch_rowmajor(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const RowMajorParams& base,
                              cudaStream_t stream) {
-  using L = RowMajorSmem<BN, STAGES>;
+  using L = RowMajorSmem<BN, STAGES, STAGED>;
   CUtensorMap ta, tb;
   const uint64_t a_dims[2] = {base.k, base.m};
   const uint64_t a_strides[1] = {uint64_t(lda) * 2};
@@ -656,16 +687,25 @@ tempo_status launch_rowmajor(const void* a, uint32_t lda, const void* w_t, uint3
   const uint32_t b_box[2] = {kBK, uint32_t(BN)};
   s = encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w_t, b_dims, b_strides, b_box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (s != TEMPO_OK) return s;
+  CUtensorMap to = ta;  // unused unless STAGED
+  if (STAGED) {
+    const uint64_t o_dims[2] = {base.n, base.m};
+    const uint64_t o_strides[1] = {uint64_t(base.ldo) * 2};
+    const uint32_t o_box[2] = {32, 32};
+    s = encode_tmap(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base.out, o_dims, o_strides, o_box,
+                    CU_TENSOR_MAP_SWIZZLE_64B);
+    if (s != TEMPO_OK) return s;
+  }
   RowMajorParams p = base;
   p.stage_tx = a_rows * kBK * 2 + L::kBBytes;
   p.m_tiles = (p.m + 127) / 128;
   p.n_tiles = (p.n + BN - 1) / BN;
   const uint32_t tiles = p.m_tiles * p.n_tiles;
   const uint32_t grid = tiles < uint32_t(sm_count()) ? tiles : uint32_t(sm_count());
-  auto kernel = gemm_rowmajor_kernel<BN, STAGES>;
+  auto kernel = gemm_rowmajor_kernel<BN, STAGES, STAGED>;
   s = set_smem(reinterpret_cast<const void*>(kernel), L::kBytes);
   if (s != TEMPO_OK) return s;
-  return launch(kernel, dim3(grid), dim3(kRowThreads), L::kBytes, stream, 1, "gemm_rowmajor_kernel", ta, tb, p);
+  return launch(kernel, dim3(grid), dim3(kRowThreads), L::kBytes, stream, 1, "gemm_rowmajor_kernel", ta, tb, to, p);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -1010,13 +1050,6 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       "[%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1)
       : "memory");
-}
-
-// A 2-D tile from this CTA's shared memory to global memory (bulk-group completion).
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t c0, int32_t c1) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
-               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(c0), "r"(c1)
-               : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
@@ -1422,9 +1455,9 @@ static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint
     return launch_pair<5>(a, lda, w_t, ldw, p, st);
   // Wide tiles when the grid still fills the GPU; narrower ones otherwise.
   const uint64_t tiles256 = uint64_t((m + 127) / 128) * ((n + 255) / 256);
-  if (tiles256 >= uint64_t(sm_count())) return launch_rowmajor<256, 4>(a, lda, w_t, ldw, p, st);
+  if (tiles256 >= uint64_t(sm_count())) return launch_rowmajor<256, 3, true>(a, lda, w_t, ldw, p, st);
   const uint64_t tiles128 = uint64_t((m + 127) / 128) * ((n + 127) / 128);
-  if (tiles128 >= uint64_t(sm_count()) / 2) return launch_rowmajor<128, 6>(a, lda, w_t, ldw, p, st);
+  if (tiles128 >= uint64_t(sm_count()) / 2) return launch_rowmajor<128, 5, true>(a, lda, w_t, ldw, p, st);
   return launch_rowmajor<64, 8>(a, lda, w_t, ldw, p, st);
 }
 

@@ -157,7 +157,7 @@ def test_block_gemm_deep_contraction_is_exact() -> None:
 # ------------------------------------------------------------------------------------------------------------
 
 @pytest.mark.parametrize(("m", "n", "k"), [(128, 256, 64), (1024, 2304, 768), (1000, 768, 768), (512, 3072, 768),
-                                           (64, 768, 3072), (300, 200, 136), (4096, 768, 3072),
+                                           (64, 768, 3072), (300, 200, 136), (4096, 768, 3072), (16000, 768, 768),
                                            # small-M shapes taking the cluster split-K path (1, 2, 4 and 8 splits)
                                            (512, 2304, 768), (512, 768, 768), (64, 2304, 768), (33, 768, 3072),
                                            (200, 3072, 768)])
