@@ -86,68 +86,6 @@ constexpr int kRowThreads = 64 + kRowEpiThreads;
 constexpr int kSplitThreads = 320;
 constexpr int kEpilogueThreads = 256;
 
-// Mean and 1/sqrt(var + eps) of `rows` rows of x (k elements, k % 8 == 0) into mean[] / rstd[], computed by the
-// `threads` threads t = 0 .. threads-1: a group of 4-32 consecutive lanes per row, each lane folding 8-element chunks
-// into a running (count, mean, M2) exactly (Chan's parallel update), the group merged by shuffles. Centred
-// variance, so large row means cost no accuracy.
-__device__ __forceinline__ void ln_row_stats(const uint16_t* x, uint32_t ldx, uint32_t k, uint32_t rows, float eps,
-                                             float* mean_out, float* rstd_out, uint32_t t, uint32_t threads) {
-  uint32_t tpr = 32;  // lanes per row: as many as cover every row (rows <= threads / 4)
-  while (tpr > 4 && rows * tpr > threads) tpr /= 2;
-  const uint32_t row = t / tpr, part = t % tpr;
-  const uint32_t chunks = k / 8;
-  float n = 0.f, mean = 0.f, m2 = 0.f;
-  if (row < rows) {
-    const uint4* xr = reinterpret_cast<const uint4*>(x + size_t(row) * ldx);
-    constexpr uint32_t kBatch = 8;
-    for (uint32_t base = part; base < chunks; base += kBatch * tpr) {
-      uint4 w[kBatch];
-#pragma unroll
-      for (uint32_t i = 0; i < kBatch; ++i) {
-        const uint32_t c = base + i * tpr;
-        w[i] = c < chunks ? __ldg(xr + c) : make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (uint32_t i = 0; i < kBatch; ++i) {
-        if (base + i * tpr >= chunks) break;
-        const uint32_t ws[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
-        float v[8], cm = 0.f;
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          v[2 * h] = bf16_lo(ws[h]);
-          v[2 * h + 1] = bf16_hi(ws[h]);
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) cm += v[j];
-        cm *= 0.125f;
-        float cm2 = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) cm2 = fmaf(v[j] - cm, v[j] - cm, cm2);
-        const float n_new = n + 8.f, delta = cm - mean;
-        mean = fmaf(delta, 8.f / n_new, mean);
-        m2 += cm2 + delta * delta * (n * 8.f / n_new);
-        n = n_new;
-      }
-    }
-  }
-  for (uint32_t off = tpr / 2; off >= 1; off /= 2) {
-    const float on = __shfl_xor_sync(0xFFFFFFFFu, n, off);
-    const float om = __shfl_xor_sync(0xFFFFFFFFu, mean, off);
-    const float o2 = __shfl_xor_sync(0xFFFFFFFFu, m2, off);
-    const float tot = n + on;
-    if (tot > 0.f) {
-      const float delta = om - mean;
-      mean = fmaf(delta, on / tot, mean);
-      m2 += o2 + delta * delta * (n * on / tot);
-      n = tot;
-    }
-  }
-  if (row < rows && part == 0) {
-    mean_out[row] = mean;
-    rstd_out[row] = rsqrtf(m2 / float(k) + eps);
-  }
-}
-
 // A 2-D tile from this CTA's shared memory to global memory (bulk-group completion).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t c0, int32_t c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
@@ -254,7 +192,72 @@ __device__ __forceinline__ void epilogue_chunk(const RowMajorParams& p, const ui
   }
 }
 
-template <int BN, int STAGES, bool STAGED>
+// A folded LayerNorm's row statistics for the 128 rows of the A operand as its k-blocks stream through the operand
+// ring (128-byte swizzled rows, 64 columns per stage): thread t (of 512) takes row t / 4 and 16 of each k-block's 64
+// columns, merges 8-element chunks exactly (Chan's update), and the four threads of a row merge by shuffles. Each
+// warp releases every stage it has read (the stage's empty barrier counts the MMA and the sixteen warps). Kept out
+// of line so its registers do not add to the epilogue's.
+__device__ __noinline__ bool ln_stats_from_stages(const uint8_t* smem, uint32_t stage_bytes, uint32_t stages,
+                                                  uint64_t* full, uint64_t* empty, uint32_t kblocks, uint32_t rows,
+                                                  uint32_t k, float eps, float* mean_out, float* rstd_out,
+                                                  uint32_t t, uint32_t lane, volatile int* abort_flag) {
+  const uint32_t srow = t >> 2, part = t & 3u;
+  float n = 0.f, mean = 0.f, m2 = 0.f;
+  uint32_t stage = 0, phase = 0;
+  bool ok = true;
+  for (uint32_t kb = 0; kb < kblocks; ++kb) {
+    if (!mbar_wait(&full[stage], phase, kWatchFull, abort_flag)) { ok = false; break; }
+    if (srow < rows) {
+      const uint8_t* a_row = smem + stage * stage_bytes + srow * 128;
+#pragma unroll
+      for (uint32_t h = 0; h < 2; ++h) {
+        const uint32_t c = 2 * part + h;  // 16-byte chunk of the row (128-byte swizzle)
+        const uint4 w = *reinterpret_cast<const uint4*>(a_row + ((c ^ (srow & 7u)) * 16));
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        float v[8], cm = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          v[2 * q] = bf16_lo(ws[q]);
+          v[2 * q + 1] = bf16_hi(ws[q]);
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) cm += v[q];
+        cm *= 0.125f;
+        float cm2 = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) cm2 = fmaf(v[q] - cm, v[q] - cm, cm2);
+        const float n_new = n + 8.f, delta = cm - mean;
+        mean = fmaf(delta, 8.f / n_new, mean);
+        m2 += cm2 + delta * delta * (n * 8.f / n_new);
+        n = n_new;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == stages) { stage = 0; phase ^= 1u; }
+  }
+  for (uint32_t off = 2; off >= 1; off /= 2) {
+    const float on = __shfl_xor_sync(0xFFFFFFFFu, n, off);
+    const float om = __shfl_xor_sync(0xFFFFFFFFu, mean, off);
+    const float o2 = __shfl_xor_sync(0xFFFFFFFFu, m2, off);
+    const float tot = n + on;
+    if (tot > 0.f) {
+      const float delta = om - mean;
+      mean = fmaf(delta, on / tot, mean);
+      m2 += o2 + delta * delta * (n * on / tot);
+      n = tot;
+    }
+  }
+  if (srow < rows && part == 0) {
+    mean_out[srow] = mean;
+    rstd_out[srow] = rsqrtf(m2 / float(k) + eps);
+  }
+  return ok;
+}
+
+// LN: the folded-LayerNorm variant (tempo_gemm_ln); a separate instantiation, so the statistics code adds no
+// registers to the others.
+template <int BN, int STAGES, bool STAGED, bool LN>
 __global__ void __launch_bounds__(kRowThreads, 1)
     gemm_rowmajor_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                          const __grid_constant__ CUtensorMap tmap_out, RowMajorParams p) {
@@ -279,9 +282,12 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
 
   if (threadIdx.x == 0) {
+    // With a folded LayerNorm the epilogue warps also read each A stage of the first tile (its rows' statistics):
+    // a stage is free once the MMA and those sixteen warps are done with it.
+    const uint32_t empty_count = LN ? 1u + kRowEpiThreads / 32 : 1u;
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], empty_count);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
@@ -395,10 +401,10 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     int32_t* exchange_idx = reinterpret_cast<int32_t*>(exchange_val + 128);
     uint32_t acc = 0, acc_phase = 0;
     pdl_wait();
-    const bool ln = (p.flags & TEMPO_GEMM_LN) != 0;
+    constexpr bool ln = LN;
     float* ln_mean = exchange_val;  // the argmax hand-off slot: the two modes are exclusive
     float* ln_rstd = exchange_val + 128;
-    uint32_t ln_block = 0xFFFFFFFFu, epi_phase = 0;
+    uint32_t ln_block = 0xFFFFFFFFu, epi_phase = 0;  // the 128-row block whose statistics are in ln_mean / ln_rstd
     // Every epilogue thread arrives; the wait is bounded, so a thread that left the loop cannot stall the others.
     auto epi_sync = [&]() -> bool {
       mbar_arrive(epi_bar);
@@ -408,17 +414,17 @@ __global__ void __launch_bounds__(kRowThreads, 1)
     };
     const bool gelu = (p.flags & TEMPO_GEMM_GELU) != 0;
     const bool argmax = (p.flags & TEMPO_GEMM_ARGMAX) != 0;
-    for (uint32_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-      if (ln && t / p.n_tiles != ln_block) {
-        // Row statistics of this tile's 128-row block, while its MMAs run (the slots are free once every epilogue
-        // thread is done with the previous block's).
-        ln_block = t / p.n_tiles;
-        if (!epi_sync()) break;
-        const uint32_t rows = p.m - ln_block * 128 < 128u ? p.m - ln_block * 128 : 128u;
-        ln_row_stats(p.ln_x + size_t(ln_block) * 128 * p.ln_ldx, p.ln_ldx, p.k, rows, p.ln_eps, ln_mean, ln_rstd,
-                     threadIdx.x - 64, kRowEpiThreads);
-        if (!epi_sync()) break;
-      }
+    if (ln && blockIdx.x < tiles) {
+      // The first tile's row statistics from its A stages as they stream in for the MMA, ready with the accumulator.
+      const uint32_t first_block = blockIdx.x / p.n_tiles;
+      const uint32_t rows = p.m - first_block * 128 < 128u ? p.m - first_block * 128 : 128u;
+      const bool ok = ln_stats_from_stages(smem, L::kStageBytes, STAGES, full, empty, kblocks, rows, p.k, p.ln_eps,
+                                           ln_mean, ln_rstd, threadIdx.x - 64, lane, abort_flag);
+      ln_block = first_block;
+      if (!ok || !epi_sync()) ln_block = 0xFFFFFFFFu;  // (a timeout: the tile loop below gives up as well)
+    }
+    // (A folded LayerNorm runs with one tile per CTA: the host guarantees it.)
+    for (uint32_t t = blockIdx.x; t < tiles && !(ln && ln_block == 0xFFFFFFFFu); t += gridDim.x) {
       if (!mbar_wait(&acc_full[acc], acc_phase, kWatchAccFull, abort_flag)) break;
       tc_fence_after();
       const uint32_t m_blk = t / p.n_tiles, n_blk = t % p.n_tiles;
@@ -669,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, int STAGES, bool STAGED = false>
+template <int BN, int STAGES, bool STAGED = false, bool LN = false>
 tempo_status launch_rowmajor(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const RowMajorParams& base,
                              cudaStream_t stream) {
   using L = RowMajorSmem<BN, STAGES, STAGED>;
@@ -702,7 +708,7 @@ tempo_status launch_rowmajor(const void* a, uint32_t lda, const void* w_t, uint3
   p.n_tiles = (p.n + BN - 1) / BN;
   const uint32_t tiles = p.m_tiles * p.n_tiles;
   const uint32_t grid = tiles < uint32_t(sm_count()) ? tiles : uint32_t(sm_count());
-  auto kernel = gemm_rowmajor_kernel<BN, STAGES, STAGED>;
+  auto kernel = gemm_rowmajor_kernel<BN, STAGES, STAGED, LN>;
   s = set_smem(reinterpret_cast<const void*>(kernel), L::kBytes);
   if (s != TEMPO_OK) return s;
   return launch(kernel, dim3(grid), dim3(kRowThreads), L::kBytes, stream, 1, "gemm_rowmajor_kernel", ta, tb, to, p);
@@ -1426,6 +1432,17 @@ static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint
     if (gemv != TEMPO_ERR_VALUE) return gemv;
   }
   if (argmax) return launch_rowmajor<256, 4>(a, lda, w_t, ldw, p, st);
+  if (ln_mode) {
+    // The folded LayerNorm takes each tile's row statistics from its own A stages, so every CTA gets one tile: the
+    // narrowest tiles (the most CTAs) that need no more tiles than SMs.
+    const uint64_t sms = uint64_t(sm_count()), m_tiles = (m + 127) / 128;
+    if (m <= 128 && k <= 1024 && (n + 15) / 16 <= sms) return launch_rowmajor<16, 8, false, true>(a, lda, w_t, ldw, p, st);
+    if (m <= 128 && k <= 1024 && (n + 31) / 32 <= sms) return launch_rowmajor<32, 8, false, true>(a, lda, w_t, ldw, p, st);
+    if (m_tiles * ((n + 63) / 64) <= sms) return launch_rowmajor<64, 8, false, true>(a, lda, w_t, ldw, p, st);
+    if (m_tiles * ((n + 127) / 128) <= sms) return launch_rowmajor<128, 5, true, true>(a, lda, w_t, ldw, p, st);
+    if (m_tiles * ((n + 255) / 256) <= sms) return launch_rowmajor<256, 3, true, true>(a, lda, w_t, ldw, p, st);
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm_ln: %u x %u needs more than one 128-row tile per SM", m, n);
+  }
   // One 128-row block with a short contraction (the decode projections of up to 128 sequences): narrow tiles over the
   // whole of K, at most one per SM, need no cross-CTA reduction.
   if (m <= 128 && k <= 1024) {

@@ -81,8 +81,10 @@ class Engine:
         capacity: cache positions per sequence (prompt + decode steps).
         device: the CUDA device.
         fold_layernorms: decode folds each block's two LayerNorms into the QKV and FC projections
-            (``ops.gemm_ln``), so a layer runs five kernels instead of seven (default: on above 8 sequences; 8 or
-            fewer rows take the CUDA-core GEMV path, which has no folded form).
+            (``ops.gemm_ln``), so a layer runs five kernels instead of seven (needs more than 8 sequences: 8 or fewer
+            rows take the CUDA-core GEMV path, which has no folded form). Default off: measured side by side on a
+            B200, the in-kernel row statistics slow the projections' operand pipeline by more than the two
+            LayerNorm launches cost (512 sequences: 460 ms of decode folded, 453 ms not; 64 sequences: 110 / 106 ms).
         decode_groups: the decode step splits the batch into this many groups of sequences, each on its own CUDA
             stream (default 1). The groups are independent, so one group's bandwidth-bound attention may overlap
             another's projections; on a B200 the extra, smaller launches cost more than the overlap gains (512
@@ -115,7 +117,7 @@ class Engine:
         self.wpe = _bf16(shared["wpe"], self.device)
         self.lnf_g = _bf16(shared["ln_f.g"], self.device)
         self.lnf_b = _bf16(shared["ln_f.b"], self.device)
-        self.fold_layernorms = batch > 8 if fold_layernorms is None else fold_layernorms
+        self.fold_layernorms = False if fold_layernorms is None else (fold_layernorms and batch > 8)
         if self.fold_layernorms:
             for lw in self.layers:
                 lw.qkv_folded = fold_layernorm(lw.ln1_g, lw.ln1_b, lw.w_qkv, lw.b_qkv)

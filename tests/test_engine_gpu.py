@@ -91,12 +91,13 @@ def test_folded_layernorm_decode_matches_the_oracle() -> None:
     layers, shared = random_gpt2(41)
     batch, prompt, steps = 12, 32, 10
     ids = np.stack([random_token_ids(300 + s, prompt) for s in range(batch)]).astype(np.int32)
-    engine = Engine(layers, shared, batch=batch, prompt=prompt, capacity=prompt + steps)
+    engine = Engine(layers, shared, batch=batch, prompt=prompt, capacity=prompt + steps, fold_layernorms=True)
     assert engine.fold_layernorms
     tokens = engine.generate(ids, steps)
     for s in range(0, batch, 3):
         _check_teacher_forced(layers, shared, ids[s], tokens[s])
-    unfolded = Engine(layers, shared, batch=batch, prompt=prompt, capacity=prompt + steps, fold_layernorms=False)
+    unfolded = Engine(layers, shared, batch=batch, prompt=prompt, capacity=prompt + steps)
+    assert not unfolded.fold_layernorms
     plain = unfolded.generate(ids, steps)
     # the two decodes may part only at a near-tie; most sequences agree throughout
     assert (plain == tokens).all(axis=1).sum() >= batch - 2

@@ -324,6 +324,18 @@ def test_gemm_ln_matches_layernorm_then_gemm(m: int, n: int, gelu: bool) -> None
     assert ops.watchdog() == 0
 
 
+def test_gemm_ln_refuses_more_tiles_than_sms() -> None:
+    """The folded LayerNorm runs one output tile per CTA; a product needing more is refused, not mis-computed."""
+    from tempo_compiler_b200 import ops
+    from tempo_compiler_b200.engine import fold_layernorm
+    x = torch.zeros((8192, 768), dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros((3072, 768), dtype=torch.bfloat16, device="cuda")
+    one = torch.ones(768, dtype=torch.bfloat16, device="cuda")
+    folded, colsum, bias_folded = fold_layernorm(one, one * 0, w, None)
+    with pytest.raises(ValueError, match="one 128-row tile per SM"):
+        ops.gemm_ln(x, folded, colsum, bias_folded)
+
+
 def test_gemm_ln_stores_keys_and_values() -> None:
     """The folded QKV projection with the decode cache store: the caches receive exactly its key and value columns."""
     from tempo_compiler_b200 import ops
