@@ -998,8 +998,8 @@ tempo_status launch_splitk(const void* a, uint32_t lda, const void* w_t, uint32_
 //   warp 0      TMA (both CTAs; .cta_group::2 copies complete on the leader's full barrier)
 //   warp 1      the leader's MMA issuer; both CTAs' warp 1 allocate and free the pair's TMEM
 //   warps 2-17  epilogue (both CTAs), each warp releasing the accumulator on the leader's barrier
-// No copy uses multicast: every CTA loads its own halves, and the leader signals the peer's barriers with
-// separate (non-multicast) commits addressed to the peer.
+// Every copy has a single destination: each CTA loads its own halves, and the leader signals the peer's barriers
+// with separate commits addressed to the peer.
 // ---------------------------------------------------------------------------------------------------------------
 
 constexpr uint32_t kPairBN = 256;
