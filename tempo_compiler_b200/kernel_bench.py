@@ -50,6 +50,7 @@ def main() -> int:
     parser.add_argument("--epilogue", choices=["plain", "bias", "gelu", "residual"], default="gelu")
     parser.add_argument("--seqs", type=int, default=64)
     parser.add_argument("--capacity", type=int, default=1152)
+    parser.add_argument("--length", type=int, default=None, help="decode: cached keys per sequence (default capacity)")
     parser.add_argument("--tokens", type=int, default=1024)
     parser.add_argument("--rows", type=int, default=65536)
     parser.add_argument("--depth", type=int, default=768)
@@ -77,11 +78,13 @@ def main() -> int:
         qkv = torch.randn((args.seqs, 3 * 768), device=dev).to(bf)
         kc = torch.randn((args.seqs, 12, args.capacity, 64), device=dev).to(bf)
         vc = torch.randn_like(kc)
-        lengths = torch.full((args.seqs,), args.capacity, dtype=torch.int32, device=dev)
+        length = args.capacity if args.length is None else args.length
+        lengths = torch.full((args.seqs,), length, dtype=torch.int32, device=dev)
         out = torch.empty((args.seqs, 768), device=dev, dtype=bf)
         ms = _time(lambda: ops.decode_attention(qkv, kc, vc, lengths, out=out), args.repeats, args.warmup)
-        nbytes = args.seqs * 12 * args.capacity * 64 * 2 * 2 + args.seqs * 3 * 768 * 2 + args.seqs * 768 * 2
-        result.update(seqs=args.seqs, capacity=args.capacity, ms=ms, bytes=nbytes, gbs=nbytes / ms / 1e6)
+        nbytes = args.seqs * 12 * length * 64 * 2 * 2 + args.seqs * 3 * 768 * 2 + args.seqs * 768 * 2
+        result.update(seqs=args.seqs, capacity=args.capacity, length=length, ms=ms,
+                      bytes=nbytes, gbs=nbytes / ms / 1e6)
     elif args.kernel == "prefill_attention":
         rows = args.seqs * args.tokens
         qkv = torch.randn((rows, 3 * 768), device=dev).to(bf)
