@@ -315,6 +315,11 @@ def _time(fn, stream, repeats: int) -> float:
     return start.elapsed_time(end) / repeats
 
 
+# DRAM traffic of decode attention per algorithmic byte, from one ncu capture of 64 sequences x 12 heads x 1152 keys:
+# 226.6 MB read + 3.5 MB written for 226.9 MB of cached keys, values, queries and outputs.
+DECODE_TRAFFIC_PER_BYTE = (226.6e6 + 3.5e6) / 226.885632e6
+
+
 def _decode_attention_roofline(engine, stream, measured, source) -> dict:
     """Decode attention over the full caches (every sequence at `capacity` keys): algorithmic bytes are each cached
     key and value read once plus the query read and the output written."""
@@ -332,12 +337,16 @@ def _decode_attention_roofline(engine, stream, measured, source) -> dict:
     achieved = algorithmic / (ms / 1000.0) / 1e9
     peak = float(measured["hbm_gbs"])
     return {"kernel": "decode_attention_kernel", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-            "frac": achieved / peak, "traffic": None, "algorithmic_bytes_per_launch": algorithmic,
+            "frac": achieved / peak, "traffic": algorithmic * DECODE_TRAFFIC_PER_BYTE,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 64-sequence launch, scaled to "
+                              "this launch by its algorithmic bytes (each key and value is read once at any size)",
+            "algorithmic_bytes_per_launch": algorithmic,
             "launch_ms": ms, "peak_source": f"{source} ({PEAKS_FILE if source == 'measured' else 'fallback'})"}
 
 
 def _gemm_roofline(engine, stream, measured, source) -> dict:
     """The prefill FC projection: M = sequences x prompt, N = 3072, K = 768, bias + exact-erf GELU epilogue."""
+    import torch
     from tempo_compiler_b200 import ops
     lw = engine.layers[0]
     fn = lambda: ops.gemm(engine.ln, lw.w_fc, bias=lw.b_fc, gelu=True, out=engine.h)  # noqa: E731
@@ -347,7 +356,11 @@ def _gemm_roofline(engine, stream, measured, source) -> dict:
     n = lw.w_fc.shape[0]
     achieved = 2.0 * m * n * k / (ms / 1000.0) / 1e12
     peak = float(measured["bf16_tflops"])
-    return {"kernel": "gemm_rowmajor_kernel (prefill FC, M=%d N=%d K=%d)" % (m, n, k), "bound": "tensor",
+    # the library's choice at this size: CTA pairs on 256 x 256 tiles once there are four tiles per pair of SMs
+    sms = torch.cuda.get_device_properties(engine.device).multi_processor_count
+    pair = -(-m // 256) * -(-n // 256) >= 4 * (sms // 2)
+    name = "gemm_pair_kernel" if pair else "gemm_rowmajor_kernel"
+    return {"kernel": "%s (prefill FC, M=%d N=%d K=%d)" % (name, m, n, k), "bound": "tensor",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak, "launch_ms": ms,
             "peak_source": f"{source} burst cuBLAS bf16"}
 

@@ -139,7 +139,12 @@ __device__ __forceinline__ void epilogue_chunk(const RowMajorParams& p, const ui
   }
   if (gelu) {
 #pragma unroll
-    for (uint32_t j = 0; j < kCW; ++j) v[j] = gelu_erf(round_bf16(v[j]));
+    for (uint32_t j = 0; j < kCW; j += 2) {
+      const uint32_t rounded = pack_bf16x2(v[j], v[j + 1]);  // one conversion rounds both
+      v[j] = bf16_lo(rounded);
+      v[j + 1] = bf16_hi(rounded);
+      gelu_erf_pair(v[j], v[j + 1]);
+    }
   }
   uint16_t* orow = p.out + size_t(row) * p.ldo;
   if (p.residual != nullptr) {
@@ -632,7 +637,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint4 w = a4[t128 * 2 + q];
           uint32_t* ws = reinterpret_cast<uint32_t*>(&w);
 #pragma unroll
-          for (int h = 0; h < 4; ++h) ws[h] = pack_bf16x2(gelu_erf(bf16_lo(ws[h])), gelu_erf(bf16_hi(ws[h])));
+          for (int h = 0; h < 4; ++h) {
+            float lo = bf16_lo(ws[h]), hi = bf16_hi(ws[h]);
+            gelu_erf_pair(lo, hi);
+            ws[h] = pack_bf16x2(lo, hi);
+          }
           a4[t128 * 2 + q] = w;
         }
         fence_proxy_async_smem();
@@ -928,7 +937,12 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       }
       if (gelu) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = gelu_erf(round_bf16(v[j]));
+        for (int j = 0; j < 8; j += 2) {
+          const uint32_t rounded = pack_bf16x2(v[j], v[j + 1]);
+          v[j] = bf16_lo(rounded);
+          v[j + 1] = bf16_hi(rounded);
+          gelu_erf_pair(v[j], v[j + 1]);
+        }
       }
       if (p.residual != nullptr) {
         const uint4 w = *reinterpret_cast<const uint4*>(p.residual + size_t(row) * p.ldr + col);

@@ -164,3 +164,23 @@ def test_weights_round_trip_through_the_reference_export_format(tmp_path) -> Non
             np.testing.assert_array_equal(original[name], loaded[name])
     for name in shared:
         np.testing.assert_array_equal(shared[name], loaded_shared[name])
+
+
+def test_gelu_constants_are_the_fit_and_meet_their_bound() -> None:
+    """The coefficients compiled into gelu_erf (common.cuh) are those fit_gelu.py derives, and their float32
+    evaluation stays within 1e-5 relative error of float64 erfc over every BF16 input with |x| <= 14."""
+    import importlib.util
+    csrc = pathlib.Path(__file__).resolve().parents[1] / "tempo_compiler_b200" / "csrc"
+    spec = importlib.util.spec_from_file_location("fit_gelu", csrc / "fit_gelu.py")
+    fit_gelu = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(fit_gelu)
+    coeffs = fit_gelu.fit()
+    body = (csrc / "common.cuh").read_text().split("float gelu_erf(float x)")[1].split("\n}\n")[0]
+    compiled = [float(v) for v in re.findall(r"fmaf\(p, t, (-?[0-9.]+)f\)", body)]
+    leading = float(re.search(r"float p = (-?[0-9.]+)f;", body).group(1))
+    assert np.array_equal(np.float32([leading] + compiled), np.float32(coeffs[::-1]))
+    x = fit_gelu.bf16_inputs()
+    ref = fit_gelu.exact(x)
+    keep = np.abs(ref / x) >= 2.0 ** -126
+    rel = np.abs(fit_gelu.evaluate_float32(x, coeffs)[keep] - ref[keep]) / np.abs(ref[keep])
+    assert rel.max() < 1e-5, rel.max()

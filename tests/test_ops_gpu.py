@@ -182,6 +182,33 @@ def test_gemm_matches_fp32_reference(m: int, n: int, k: int, epilogue: str) -> N
     assert torch.isfinite(out.float()).all()
 
 
+@pytest.mark.parametrize("m_extra", [0, 60000])
+def test_gemm_gelu_on_every_bf16_input(m_extra: int) -> None:
+    """GELU's input is the BF16-rounded sum, so every finite BF16 value with |x| <= 14 (the rows of A, times an
+    identity weight) covers all its inputs; beyond 14 GELU(x) is x or a value flushed to zero. Against float64
+    erfc: correctly rounded for all but a handful, never more than one BF16 step off. m_extra pads M with zero rows
+    so the prefill kernels run it too."""
+    from tempo_compiler_b200 import ops
+    bits = (torch.arange(1 << 16, dtype=torch.int32) << 16).view(torch.float32)
+    x = bits[torch.isfinite(bits) & (bits.abs() <= 14) & (bits.abs() >= 1e-30)]
+    cols = 128
+    rows = (x.numel() + cols - 1) // cols
+    a = torch.zeros(rows * cols + m_extra * cols)
+    a[:x.numel()] = x
+    a = a.view(-1, cols).to(torch.bfloat16).cuda()
+    eye = torch.eye(cols, dtype=torch.bfloat16, device="cuda")
+    out = ops.gemm(a, eye, gelu=True).flatten()[:x.numel()].cpu()
+    xd = x.double()
+    exact = 0.5 * xd * torch.special.erfc(-xd / math.sqrt(2.0))
+    want = exact.to(torch.bfloat16)
+    normal = (exact / xd).abs() >= 2.0 ** -126  # Phi(x) below the smallest normal float flushes to zero
+    assert (out[~normal].float().abs() <= x[~normal].abs() * 2.0 ** -126).all()
+    as_int = lambda t: t.view(torch.int16).int()
+    steps = (as_int(out) - as_int(want)).abs()[normal]
+    assert steps.max().item() <= 1, float(x[normal][steps.argmax()])
+    assert (steps > 0).sum().item() <= 16, (steps > 0).sum().item()
+
+
 @pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
 @pytest.mark.parametrize(("n", "k"), [(2304, 768), (768, 3072), (200, 136)])
 @pytest.mark.parametrize("epilogue", ["bias", "gelu", "residual"])
