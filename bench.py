@@ -336,8 +336,14 @@ def _decode_attention_roofline(engine, stream, measured, source) -> dict:
         engine.batch * heads * head * 2
     achieved = algorithmic / (ms / 1000.0) / 1e9
     peak = float(measured["hbm_gbs"])
+    # the streaming-read ceiling of this GPU, measured beside it: 2 GiB read once per launch by the calibration kernel
+    src = torch.empty(2 << 30, dtype=torch.uint8, device=engine.device)
+    sink = ops.stream_read(src)
+    read_ms = _time(lambda: ops.stream_read(src, sink), stream, 10)
+    read_gbs = (2 << 30) / (read_ms / 1000.0) / 1e9
+    del src, sink
     return {"kernel": "decode_attention_kernel", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-            "frac": achieved / peak, "traffic": algorithmic * DECODE_TRAFFIC_PER_BYTE,
+            "frac": achieved / peak, "read_ceiling_gbs": read_gbs, "frac_of_read_ceiling": achieved / read_gbs, "traffic": algorithmic * DECODE_TRAFFIC_PER_BYTE,
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one 64-sequence launch, scaled to "
                               "this launch by its algorithmic bytes (each key and value is read once at any size)",
             "algorithmic_bytes_per_launch": algorithmic,

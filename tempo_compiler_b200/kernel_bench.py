@@ -7,6 +7,7 @@ It allocates only that kernel's operands, so a profiler capture of it stays smal
     python -m tempo_compiler_b200.kernel_bench prefill_attention --seqs 8 --tokens 1024
     python -m tempo_compiler_b200.kernel_bench layernorm --rows 65536
     python -m tempo_compiler_b200.kernel_bench block_gemm --depth 768 --columns 3072
+    python -m tempo_compiler_b200.kernel_bench stream_read --gib 2
 
 Prints one JSON line: the launch time and the achieved rate against the algorithmic work.
 """
@@ -43,7 +44,9 @@ def _time(fn, repeats: int, warmup: int) -> float:
 
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("kernel", choices=["gemm", "decode_attention", "prefill_attention", "layernorm", "block_gemm"])
+    parser.add_argument("kernel", choices=["gemm", "decode_attention", "prefill_attention", "layernorm", "block_gemm",
+                                           "stream_read"])
+    parser.add_argument("--gib", type=float, default=2.0, help="stream_read: GiB read per launch")
     parser.add_argument("--m", type=int, default=65536)
     parser.add_argument("--n", type=int, default=3072)
     parser.add_argument("--k", type=int, default=768)
@@ -100,6 +103,12 @@ def main() -> int:
         ms = _time(lambda: ops.layernorm(x, g, b, out=out), args.repeats, args.warmup)
         nbytes = 2 * args.rows * 768 * 2
         result.update(rows=args.rows, ms=ms, bytes=nbytes, gbs=nbytes / ms / 1e6)
+    elif args.kernel == "stream_read":
+        nbytes = int(args.gib * (1 << 30)) // 16 * 16
+        src = torch.empty(nbytes, dtype=torch.uint8, device=dev).random_(0, 255)
+        sink = ops.stream_read(src)
+        ms = _time(lambda: ops.stream_read(src, sink), args.repeats, args.warmup)
+        result.update(bytes=nbytes, ms=ms, gbs=nbytes / ms / 1e6)
     else:
         acts = torch.randint(-2000, 2000, (args.depth * 32,), dtype=torch.int16, device=dev)
         weights = torch.randint(-2000, 2000, (args.depth * args.columns,), dtype=torch.int16, device=dev)

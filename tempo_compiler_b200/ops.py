@@ -7,6 +7,8 @@ a wrong dtype or a missing library raises.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from tempo_compiler_b200 import lib as _lib
@@ -221,3 +223,19 @@ def watchdog() -> int:
     code = ctypes.c_int32()
     _lib.call("tempo_watchdog", ctypes.byref(code))
     return int(code.value)
+
+
+def stream_read(src: torch.Tensor, sink: torch.Tensor | None = None) -> torch.Tensor:
+    """Calibration: streams `src` (a contiguous device tensor) once through the HBM read path; returns the sink the
+    kernel folds it into. Its rate is the read ceiling of the bandwidth-bound kernels."""
+    if not src.is_contiguous():
+        raise ValueError("stream_read needs a contiguous source")
+    threads = ctypes.c_uint32()
+    _lib.call("tempo_stream_read_threads", ctypes.byref(threads))
+    if sink is None:
+        sink = torch.empty(threads.value * 16, dtype=torch.uint8, device=src.device)
+    elif sink.numel() * sink.element_size() < threads.value * 16:
+        raise ValueError("stream_read sink too small")
+    _launch("tempo_stream_read", src.data_ptr(), src.numel() * src.element_size(), sink.data_ptr(), _stream())
+    return sink
+

@@ -209,6 +209,21 @@ def test_gemm_gelu_on_every_bf16_input(m_extra: int) -> None:
     assert (steps > 0).sum().item() <= 16, (steps > 0).sum().item()
 
 
+def test_stream_read_folds_every_word() -> None:
+    """The calibration read touches every word of a source of whole groups: the XOR of its sink words is the XOR of
+    all source words."""
+    import ctypes
+    from tempo_compiler_b200 import lib, ops
+    threads = ctypes.c_uint32()
+    lib.call("tempo_stream_read_threads", ctypes.byref(threads))
+    words = threads.value * 8 * 3
+    src = torch.randint(-2**31, 2**31 - 1, (words * 4,), dtype=torch.int32, device="cuda")
+    sink = ops.stream_read(src)
+    torch.cuda.synchronize()
+    fold = lambda t: np.bitwise_xor.reduce(t.cpu().numpy().view(np.uint32).reshape(-1, 4), axis=0)  # noqa: E731
+    np.testing.assert_array_equal(fold(sink), fold(src))
+
+
 @pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
 @pytest.mark.parametrize(("n", "k"), [(2304, 768), (768, 3072), (200, 136)])
 @pytest.mark.parametrize("epilogue", ["bias", "gelu", "residual"])
