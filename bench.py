@@ -15,6 +15,7 @@ Prints one JSON line on rank 0.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -94,9 +95,20 @@ def cpu_sample(args, layers, shared) -> tuple[float, int]:
     return time.perf_counter() - started, args.cpu_prompt + args.cpu_decode
 
 
+def all_host_threads() -> None:
+    """Lets the BLAS pool use every core this process may run on (torchrun starts each rank with
+    OMP_NUM_THREADS=1; the reference arm runs on rank 0 alone)."""
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=len(os.sched_getaffinity(0)), user_api="blas")
+    except Exception:  # noqa: BLE001
+        pass
+
+
 def reference_arm(args) -> int:
     if int(os.environ.get("RANK", "0")) != 0:
         return 0
+    all_host_threads()
     from tempo_compiler_b200.weights import random_gpt2
     layers, shared = random_gpt2(args.seed)
     for _ in range(args.warmup):
@@ -126,34 +138,56 @@ def reference_arm(args) -> int:
 # ---------------------------------------------------------------------------------------------------------------
 
 class Clocks:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
+    """nvidia-smi sampling of the job's GPUs every 100 ms. Each sample carries nvidia-smi's own timestamp, so only the
+    samples taken inside the timed region count, whatever the pipe's buffering."""
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int) -> None:
-        self.index = index
+    def __init__(self, indices: list[int]) -> None:
+        self.indices = indices
         self.proc = None
         self.lines: list[str] = []
         self.thread = None
+        self.t_start = self.t_end = 0.0
 
     def start(self) -> "Clocks":
+        """Starts the sampler and waits (up to 10 s) for its first sample, so the timed region is covered."""
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.index)], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
+                                          "-lms", "100", "-i", ",".join(str(i) for i in self.indices)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except OSError:
             self.proc = None
+            return self
+        deadline = time.time() + 10.0
+        while not self.lines and time.time() < deadline and self.proc.poll() is None:
+            time.sleep(0.02)
         return self
 
     def _read(self) -> None:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def mark_start(self) -> None:
+        self.t_start = time.time()
+
+    def mark_end(self) -> None:
+        self.t_end = time.time()
+
+    @staticmethod
+    def _stamp(text: str) -> float | None:
+        try:
+            return datetime.datetime.strptime(text, "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            return None
+
     def stop(self) -> dict | None:
         if self.proc is None:
             return None
+        time.sleep(0.25)  # the sample that closes the region
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -161,23 +195,35 @@ class Clocks:
             self.proc.kill()
         if self.thread is not None:
             self.thread.join(timeout=2)
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
+            stamp = self._stamp(parts[0])
             try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
+                rows.append((stamp, float(parts[2]), float(parts[3]), parts[6:10]))
             except ValueError:
                 continue
-            for name, value in zip(names, parts[5:9]):
-                if value.lower() == "active":
-                    reasons.add(name)
-        if not sm:
+        inside = [r for r in rows if r[0] is not None and self.t_start - 0.05 <= r[0] <= self.t_end + 0.05]
+        used = inside or [r for r in rows if r[0] is not None and r[0] >= self.t_start][:len(self.indices)]
+        if not used:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = {name for r in used for name, value in zip(names, r[3]) if value.lower() == "active"}
+        return {"sm_mhz": statistics.median(r[1] for r in used), "sm_max_mhz": max(r[2] for r in used),
+                "reasons": sorted(reasons), "samples": len(used), "gpus": len(self.indices),
+                "in_timed_region": bool(inside)}
+
+
+def _job_gpu_indices(world: int) -> list[int]:
+    """nvidia-smi indices of local ranks 0 .. world - 1 (one rank per GPU on one node)."""
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if visible:
+        ids = [v.strip() for v in visible.split(",") if v.strip()]
+        if all(v.isdigit() for v in ids) and len(ids) >= world:
+            return [int(v) for v in ids[:world]]
+    return list(range(world))
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -239,14 +285,20 @@ def b200_arm(args) -> int:
 
     stream = torch.cuda.current_stream(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = Clocks(local).start()
+    clocks = Clocks(_job_gpu_indices(world)).start() if rank == 0 else None
+    barrier()
+    torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.mark_start()
     start.record(stream)
     for _ in range(args.steps):
         engine.run(ids_dev, args.decode, graph=graph)
     end.record(stream)
     torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.mark_end()
     barrier()
-    clock_info = clocks.stop()
+    clock_info = clocks.stop() if clocks is not None else None
     ms = max_over_ranks(start.elapsed_time(end))
     tokens_per_step = args.sequences * (args.prompt + args.decode)
     value = tokens_per_step * args.steps / (ms / 1000.0)
