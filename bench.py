@@ -48,6 +48,9 @@ def parse() -> argparse.Namespace:
     p.add_argument("--no-graph", action="store_true", help="eager decode instead of the captured CUDA graph")
     p.add_argument("--fold-layernorms", choices=["auto", "on", "off"], default="auto",
                    help="decode with the LayerNorms folded into the projections (default: the engine's choice)")
+    p.add_argument("--fuse-small-norms", choices=["auto", "on", "off"], default="auto",
+                   help="decode groups of at most 8 sequences normalise inside their projections (default: the "
+                        "engine's choice)")
     p.add_argument("--decode-groups", type=int, default=None,
                    help="independent sequence groups per decode step, one CUDA stream each (default: the engine's)")
     return p.parse_args()
@@ -267,7 +270,8 @@ def b200_arm(args) -> int:
     ids = ids.astype(np.int32)
     engine = Engine(layers, shared, batch=per_rank, prompt=args.prompt, capacity=args.prompt + args.decode,
                     device=device, decode_groups=args.decode_groups,
-                    fold_layernorms=None if args.fold_layernorms == "auto" else args.fold_layernorms == "on")
+                    fold_layernorms=None if args.fold_layernorms == "auto" else args.fold_layernorms == "on",
+                    fuse_small_norms=None if args.fuse_small_norms == "auto" else args.fuse_small_norms == "on")
     ids_dev = torch.from_numpy(ids).to(device)
     graph = not args.no_graph
 
@@ -334,7 +338,8 @@ def b200_arm(args) -> int:
                 "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded uniform token ids, random-init weights ~N(0,0.02))",
                 "config": {**workload(args), "decode_groups_per_gpu": len(engine.decode_groups),
-                           "layernorms_folded_in_decode": engine.fold_layernorms},
+                           "layernorms_folded_in_decode": engine.fold_layernorms,
+                           "layernorms_inside_small_decode_projections": engine.fuse_small_norms},
                 "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches_per_step * args.steps * world,
                 "clocks": clock_info, "roofline": roof, "gemm_roofline": gemm_roof,

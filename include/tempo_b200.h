@@ -183,6 +183,21 @@ tempo_status tempo_gemm_qkv(const void* a, uint32_t lda, const void* w_t, uint32
                             uint32_t heads, uint32_t head, uint32_t capacity, uint32_t tokens_per_seq,
                             const int32_t* positions, void* stream);
 
+/* LayerNorm then projection for at most 8 rows, in one launch: layernorm_resident followed by gemm_resident
+ * (board_package/gpt2_inference.py:474-503 and :574-640). Every CTA normalises the M rows of x (gamma, beta, epsilon,
+ * the arithmetic of tempo_layernorm) into its shared memory and streams its weight columns against them, so the
+ * result has exactly the bits of tempo_layernorm followed by tempo_gemm (or tempo_gemm_qkv with positions) and no
+ * normalised copy is written. For decode with a handful of sequences, where each launch costs more than its work.
+ * 1 <= M <= 8, K (the features) a multiple of 8 up to 1024. flags: 0, TEMPO_GEMM_GELU, or TEMPO_GEMM_ARGMAX (the
+ * final LayerNorm before the LM head; part_val / part_idx as tempo_gemm's). With k_cache / v_cache non-NULL the key
+ * and value columns are stored into the caches as tempo_gemm_qkv stores them in decode (row r is sequence r at
+ * positions[r]; N == 3 * heads * head). */
+tempo_status tempo_gemm_norm(const void* x, uint32_t ldx, const void* gamma, const void* beta, float epsilon,
+                             const void* w_t, uint32_t ldw, const void* bias, void* out, uint32_t ldo, uint32_t m,
+                             uint32_t n, uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx, void* k_cache,
+                             void* v_cache, uint32_t heads, uint32_t head, uint32_t capacity,
+                             const int32_t* positions, void* stream);
+
 /* A projection with the LayerNorm before it folded in: layernorm_resident followed by gemm_resident
  * (board_package/gpt2_inference.py:474-503 and :574-640) as one kernel, for the decode step. With wg = gamma x W
  * (w_t_folded[N, K] is W^T with column k scaled by gamma[k], BF16), colsum[n] = sum_k wg[n, k] (FP32, of the BF16

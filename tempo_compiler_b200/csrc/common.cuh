@@ -392,6 +392,70 @@ __device__ __forceinline__ uint16_t* kv_destination(const KvStore& kv, uint32_t 
 __device__ __forceinline__ uint32_t warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
 
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& w, float (&f)[8]) {
+  f[0] = bf16_lo(w.x); f[1] = bf16_hi(w.x); f[2] = bf16_lo(w.y); f[3] = bf16_hi(w.y);
+  f[4] = bf16_lo(w.z); f[5] = bf16_hi(w.z); f[6] = bf16_lo(w.w); f[7] = bf16_hi(w.w);
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 w;
+  w.x = pack_bf16x2(f[0], f[1]); w.y = pack_bf16x2(f[2], f[3]);
+  w.z = pack_bf16x2(f[4], f[5]); w.w = pack_bf16x2(f[6], f[7]);
+  return w;
+}
+
+// One row's LayerNorm by one warp: lane l holds the row's 16-byte chunks l, l + 32, ... (up to CPL of them, `features`
+// / 8 in all); mean, centred variance, rsqrt(var + epsilon), then (x - mean) rstd gamma + beta rounded to BF16 into
+// `orow` (global or shared memory). The standalone LayerNorm and the small-M projections that normalise their own
+// input share it, so both produce the same bits; a larger CPL than needed only skips chunks, in the same order.
+template <int CPL>
+__device__ __forceinline__ void layernorm_row(const uint16_t* __restrict__ xr, const uint16_t* __restrict__ gamma,
+                                              const uint16_t* __restrict__ beta, uint32_t features, float epsilon,
+                                              uint16_t* orow) {
+  const uint32_t lane = lane_id();
+  const uint32_t chunks = features / 8;
+  float v[CPL][8];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const uint32_t c = lane + 32u * i;
+    if (c < chunks) {
+      unpack8(*reinterpret_cast<const uint4*>(xr + c * 8), v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += v[i][j];
+    }
+  }
+  const float inv_f = 1.0f / float(features);
+  const float mean = warp_sum(sum) * inv_f;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    if (lane + 32u * i < chunks) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sq += (v[i][j] - mean) * (v[i][j] - mean);
+    }
+  }
+  const float scale = rsqrtf(warp_sum(sq) * inv_f + epsilon);
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const uint32_t c = lane + 32u * i;
+    if (c < chunks) {
+      float g[8], b[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(gamma + c * 8)), g);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(beta + c * 8)), b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = (v[i][j] - mean) * scale * g[j] + b[j];
+      *reinterpret_cast<uint4*>(orow + c * 8) = pack8(v[i]);
+    }
+  }
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

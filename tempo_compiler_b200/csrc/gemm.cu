@@ -25,11 +25,13 @@ namespace tempo {
 
 TEMPO_WATCHDOG_READER(watchdog_gemm)
 
-// gemv.cu: the bandwidth-bound path for at most 8 rows (TEMPO_ERR_VALUE when it does not apply).
+// gemv.cu: the bandwidth-bound path for at most 8 rows (TEMPO_ERR_VALUE when it does not apply), optionally
+// normalising its input rows first (LayerNorm with gamma, beta, epsilon; K <= 1024).
 tempo_status gemv_dispatch(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
                            const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m, uint32_t n,
                            uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx, const KvStore& kv,
-                           cudaStream_t stream);
+                           cudaStream_t stream, const uint16_t* ln_gamma = nullptr, const uint16_t* ln_beta = nullptr,
+                           float ln_eps = 0.f);
 
 namespace {
 
@@ -1397,6 +1399,44 @@ extern "C" tempo_status tempo_gemm_ln(const void* x, uint32_t ldx, const void* w
   }
   return gemm_impl(x, ldx, w_t_folded, ldw, nullptr, nullptr, 0, out, ldo, m, n, k, flags | TEMPO_GEMM_LN, nullptr,
                    nullptr, kv, LnFold{colsum, bias_folded, epsilon}, stream);
+}
+
+extern "C" tempo_status tempo_gemm_norm(const void* x, uint32_t ldx, const void* gamma, const void* beta,
+                                        float epsilon, const void* w_t, uint32_t ldw, const void* bias, void* out,
+                                        uint32_t ldo, uint32_t m, uint32_t n, uint32_t k, uint32_t flags,
+                                        float* part_val, int32_t* part_idx, void* k_cache, void* v_cache,
+                                        uint32_t heads, uint32_t head, uint32_t capacity, const int32_t* positions,
+                                        void* stream) {
+  if (m == 0 || m > 8 || n == 0 || k == 0 || k > 1024 || k % 8 || ldx % 8 || ldx < k || ldw % 8 || ldw < k)
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm_norm: M %u (1..8) N %u K %u (8..1024, multiple of 8) strides %u %u", m,
+                n, k, ldx, ldw);
+  if (!aligned16(x) || !aligned16(gamma) || !aligned16(beta) || !aligned16(w_t) ||
+      (bias != nullptr && !aligned16(bias)))
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm_norm: operands must be 16-byte aligned");
+  if (flags & ~(TEMPO_GEMM_GELU | TEMPO_GEMM_ARGMAX))
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm_norm: only TEMPO_GEMM_GELU or TEMPO_GEMM_ARGMAX may be set");
+  const bool argmax = (flags & TEMPO_GEMM_ARGMAX) != 0;
+  if (argmax && (part_val == nullptr || part_idx == nullptr))
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm_norm: argmax mode needs the partial buffers");
+  if (!argmax && (out == nullptr || ldo < n || ldo % 8 || !aligned16(out)))
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm_norm: output must be 16-byte aligned with a row stride >= N, multiple of 8");
+  KvStore kv{};
+  if (k_cache != nullptr || v_cache != nullptr) {
+    const uint32_t width = heads * head;
+    if (k_cache == nullptr || v_cache == nullptr || !aligned16(k_cache) || !aligned16(v_cache) || positions == nullptr)
+      return fail(TEMPO_ERR_VALUE, "tempo_gemm_norm: the cache store needs both caches (16-byte aligned) and positions");
+    if (heads == 0 || head == 0 || head % 32 || capacity == 0 || n != 3 * width)
+      return fail(TEMPO_ERR_VALUE, "tempo_gemm_norm: heads %u head %u (multiple of 32) capacity %u, N %u", heads, head,
+                  capacity, n);
+    kv = KvStore{static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), positions, 0, m, heads, head,
+                 capacity, width};
+  }
+  const tempo_status s = gemv_dispatch(x, ldx, w_t, ldw, bias, nullptr, 0, out, ldo, m, n, k, flags, part_val,
+                                       part_idx, kv, static_cast<cudaStream_t>(stream),
+                                       static_cast<const uint16_t*>(gamma), static_cast<const uint16_t*>(beta),
+                                       epsilon);
+  if (s == TEMPO_ERR_VALUE) return fail(TEMPO_ERR_VALUE, "tempo_gemm_norm: %u x %u x %u does not fit the kernel", m, n, k);
+  return s;
 }
 
 static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,

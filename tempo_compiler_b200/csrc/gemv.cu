@@ -26,12 +26,14 @@ struct GemvParams {
   int32_t* part_idx;
   uint32_t m, n, k, lda, ldw, ldr, ldo, flags, tiles;
   KvStore kv;
+  // Optional LayerNorm of the input rows (gamma non-null): every CTA normalises the M rows of `a` itself, exactly as
+  // the standalone LayerNorm would, into its shared-memory copy of the activations.
+  const uint16_t* ln_gamma;
+  const uint16_t* ln_beta;
+  float ln_eps;
 };
 
-__device__ __forceinline__ void unpack8(const uint4& w, float (&f)[8]) {
-  f[0] = bf16_lo(w.x); f[1] = bf16_hi(w.x); f[2] = bf16_lo(w.y); f[3] = bf16_hi(w.y);
-  f[4] = bf16_lo(w.z); f[5] = bf16_hi(w.z); f[6] = bf16_lo(w.w); f[7] = bf16_hi(w.w);
-}
+constexpr uint32_t kNormMaxK = 1024;  // rows a warp normalises from registers: 4 chunks of 8 per lane
 
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
@@ -97,9 +99,16 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(GemvParams p) {
   pdl_launch_dependents();
   pdl_wait();
 
-  for (uint32_t i = threadIdx.x; i < p.m * (p.k / 8); i += blockDim.x) {
-    const uint32_t r = i / (p.k / 8), ch = i % (p.k / 8);
-    reinterpret_cast<uint4*>(a_smem)[i] = *reinterpret_cast<const uint4*>(p.a + size_t(r) * p.lda + ch * 8);
+  if (p.ln_gamma != nullptr) {
+    // warp r normalises row r (M <= 8 = warps)
+    if (warp < p.m)
+      layernorm_row<kNormMaxK / 256>(p.a + size_t(warp) * p.lda, p.ln_gamma, p.ln_beta, p.k, p.ln_eps,
+                                     a_smem + size_t(warp) * p.k);
+  } else {
+    for (uint32_t i = threadIdx.x; i < p.m * (p.k / 8); i += blockDim.x) {
+      const uint32_t r = i / (p.k / 8), ch = i % (p.k / 8);
+      reinterpret_cast<uint4*>(a_smem)[i] = *reinterpret_cast<const uint4*>(p.a + size_t(r) * p.lda + ch * 8);
+    }
   }
   __syncthreads();
 
@@ -175,8 +184,9 @@ tempo_status launch_gemv(const GemvParams& p, cudaStream_t stream) {
 tempo_status gemv_dispatch(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
                            const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m, uint32_t n,
                            uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx, const KvStore& kv,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, const uint16_t* ln_gamma, const uint16_t* ln_beta, float ln_eps) {
   if (m == 0 || m > 8 || k % 8 || size_t(m) * k * 2 > 96 * 1024) return TEMPO_ERR_VALUE;
+  if (ln_gamma != nullptr && (k > kNormMaxK || ln_beta == nullptr || lda % 8)) return TEMPO_ERR_VALUE;
   GemvParams p{};
   p.a = static_cast<const uint16_t*>(a);
   p.w = static_cast<const uint16_t*>(w_t);
@@ -195,6 +205,9 @@ tempo_status gemv_dispatch(const void* a, uint32_t lda, const void* w_t, uint32_
   p.flags = flags;
   p.tiles = (n + kArgmaxTile - 1) / kArgmaxTile;
   p.kv = kv;
+  p.ln_gamma = ln_gamma;
+  p.ln_beta = ln_beta;
+  p.ln_eps = ln_eps;
   if (m == 1) return launch_gemv<1>(p, stream);
   if (m == 2) return launch_gemv<2>(p, stream);
   if (m <= 4) return launch_gemv<4>(p, stream);

@@ -89,11 +89,15 @@ class Engine:
             stream (default 1). The groups are independent, so one group's bandwidth-bound attention may overlap
             another's projections; on a B200 the extra, smaller launches cost more than the overlap gains (512
             sequences: 453 ms of decode with one group, 483 with two, 519 with four), hence the default.
+        fuse_small_norms: decode groups of at most 8 sequences compute each LayerNorm inside the projection that
+            follows it (``ops.gemm_norm``, the same bits as the separate kernels): five kernels per layer instead of
+            seven, and the final LayerNorm inside the LM head. Default on.
     """
 
     def __init__(self, layers: list[dict], shared: dict, *, batch: int, prompt: int, capacity: int,
                  shape: GPT2Shape = GPT2_SMALL, device: str | torch.device = "cuda",
-                 decode_groups: int | None = None, fold_layernorms: bool | None = None) -> None:
+                 decode_groups: int | None = None, fold_layernorms: bool | None = None,
+                 fuse_small_norms: bool | None = None) -> None:
         if not torch.cuda.is_available():
             raise RuntimeError("the B200 engine needs a CUDA device; there is no CPU path")
         self.device = torch.device(device)
@@ -118,6 +122,9 @@ class Engine:
         self.lnf_g = _bf16(shared["ln_f.g"], self.device)
         self.lnf_b = _bf16(shared["ln_f.b"], self.device)
         self.fold_layernorms = False if fold_layernorms is None else (fold_layernorms and batch > 8)
+        # decode groups of at most 8 sequences normalise inside their projections (tempo_gemm_norm: same bits, two
+        # launches fewer per layer and one fewer per step)
+        self.fuse_small_norms = True if fuse_small_norms is None else fuse_small_norms
         if self.fold_layernorms:
             for lw in self.layers:
                 lw.qkv_folded = fold_layernorm(lw.ln1_g, lw.ln1_b, lw.w_qkv, lw.b_qkv)
@@ -167,6 +174,9 @@ class Engine:
         if decode and self.fold_layernorms:
             self._folded_decode_layer(lw, index, x, qkv, attn, h, seqs)
             return
+        if decode and self._fused_norms(x):
+            self._normalising_decode_layer(lw, index, x, qkv, attn, h, seqs)
+            return
         ops.layernorm(x, lw.ln1_g, lw.ln1_b, epsilon=LN_EPSILON, out=ln)
         # the projection's epilogue also writes this step's keys and values into the layer's cache
         k_cache, v_cache = self.k_cache[index][seqs], self.v_cache[index][seqs]
@@ -180,6 +190,20 @@ class Engine:
         ops.gemm(attn, lw.w_proj, bias=lw.b_proj, residual=x, out=x)
         ops.layernorm(x, lw.ln2_g, lw.ln2_b, epsilon=LN_EPSILON, out=ln)
         ops.gemm(ln, lw.w_fc, bias=lw.b_fc, gelu=True, out=h)
+        ops.gemm(h, lw.w_out, bias=lw.b_out, residual=x, out=x)
+
+    def _fused_norms(self, x) -> bool:
+        return self.fuse_small_norms and x.shape[0] <= 8
+
+    def _normalising_decode_layer(self, lw: LayerWeights, index: int, x, qkv, attn, h, seqs: slice) -> None:
+        """One decode block of at most 8 sequences, each LayerNorm computed inside the projection after it."""
+        k_cache, v_cache = self.k_cache[index][seqs], self.v_cache[index][seqs]
+        positions = self.positions[seqs]
+        ops.gemm_norm(x, lw.ln1_g, lw.ln1_b, lw.w_qkv, epsilon=LN_EPSILON, bias=lw.b_qkv, out=qkv, k_cache=k_cache,
+                      v_cache=v_cache, positions=positions)
+        ops.decode_attention(qkv, k_cache, v_cache, positions, length_offset=1, out=attn)
+        ops.gemm(attn, lw.w_proj, bias=lw.b_proj, residual=x, out=x)
+        ops.gemm_norm(x, lw.ln2_g, lw.ln2_b, lw.w_fc, epsilon=LN_EPSILON, bias=lw.b_fc, gelu=True, out=h)
         ops.gemm(h, lw.w_out, bias=lw.b_out, residual=x, out=x)
 
     def _folded_decode_layer(self, lw: LayerWeights, index: int, x, qkv, attn, h, seqs: slice) -> None:
@@ -221,8 +245,14 @@ class Engine:
         ops.embed(self.ids[seqs], self.positions[seqs], self.wte, self.wpe, out=dx)
         for index, lw in enumerate(self.layers):
             self._layer(lw, index, dx, dln, dqkv, dattn, dh, decode=True, seqs=seqs)
-        ops.layernorm(dx, self.lnf_g, self.lnf_b, epsilon=LN_EPSILON, out=dln)
         # the token decoded at position p is generated token p - prompt + 1
+        if self._fused_norms(dx):
+            ops.gemm_norm(dx, self.lnf_g, self.lnf_b, self.wte, epsilon=LN_EPSILON, part_val=self.part_val[seqs],
+                          part_idx=self.part_idx[seqs])
+            ops.argmax_finish(self.part_val[seqs], self.part_idx[seqs], self.ids[seqs], tokens_out=self.tokens[seqs],
+                              positions=self.positions[seqs], index_offset=1 - self.prompt, advance=1)
+            return
+        ops.layernorm(dx, self.lnf_g, self.lnf_b, epsilon=LN_EPSILON, out=dln)
         self._head(index_offset=1 - self.prompt, advance=1, seqs=seqs)
 
     def _decode_step(self) -> None:

@@ -68,6 +68,8 @@ _SIGNATURES = {
     "tempo_decode_attention": [_vp, _vp, _vp, _vp, _i32, _vp, _u32, _u32, _u32, _u32, _vp],
     "tempo_argmax_finish": [_vp, _vp, _u32, _u32, _vp, _vp, _u32, _vp, _i32, _i32, _vp],
     "tempo_lm_head_argmax_noalloc": [_vp, _u32, _vp, _u32, _u32, _u32, _u32, _vp, _vp],
+    "tempo_gemm_norm": [_vp, _u32, _vp, _vp, _f32, _vp, _u32, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp, _vp,
+                        _vp, _u32, _u32, _u32, _vp, _vp],
     "tempo_stream_read_threads": [ctypes.POINTER(_u32)],
     "tempo_stream_read": [_vp, _u64, _vp, _vp],
 }

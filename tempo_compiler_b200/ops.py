@@ -113,6 +113,33 @@ def gemm_ln(x: torch.Tensor, w_folded: torch.Tensor, colsum: torch.Tensor, bias_
     return out
 
 
+def gemm_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, w_t: torch.Tensor, *, epsilon: float = 1e-5,
+              bias: torch.Tensor | None = None, gelu: bool = False, out: torch.Tensor | None = None,
+              k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None,
+              positions: torch.Tensor | None = None, part_val: torch.Tensor | None = None,
+              part_idx: torch.Tensor | None = None) -> torch.Tensor | None:
+    """LayerNorm(x) then the projection, one launch for at most 8 rows: the bits of layernorm() followed by gemm()
+    (gemm_qkv with the caches and positions; gemm_argmax with the partial buffers, returning None)."""
+    _check(x, torch.bfloat16, "x")
+    _check(w_t, torch.bfloat16, "w_t")
+    m, k = x.shape
+    n = w_t.shape[0]
+    if w_t.shape[1] != k:
+        raise ValueError(f"inner dimensions differ: x {tuple(x.shape)}, w_t {tuple(w_t.shape)}")
+    argmax = part_val is not None
+    if not argmax and out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    heads = head = capacity = 0
+    if k_cache is not None:
+        _, heads, capacity, head = k_cache.shape
+    flags = _lib.GEMM_ARGMAX if argmax else (_lib.GEMM_GELU if gelu else 0)
+    _launch("tempo_gemm_norm", x.data_ptr(), x.stride(0), gamma.data_ptr(), beta.data_ptr(), float(epsilon),
+            w_t.data_ptr(), w_t.stride(0), _ptr(bias), _ptr(out), out.stride(0) if out is not None else n, m, n, k,
+            flags, _ptr(part_val), _ptr(part_idx), _ptr(k_cache), _ptr(v_cache), heads, head, capacity,
+            _ptr(positions), _stream())
+    return None if argmax else out
+
+
 def gemm_argmax(a: torch.Tensor, w_t: torch.Tensor, part_val: torch.Tensor, part_idx: torch.Tensor) -> None:
     """Per-row (max, first argmax) of a @ w_t^T over each 256-column tile into the partial buffers [M, ceil(N/256)]."""
     _check(a, torch.bfloat16, "a")

@@ -118,6 +118,23 @@ def test_grouped_decode_matches_the_oracle() -> None:
     np.testing.assert_array_equal(engine.generate(ids, steps, graph=False), tokens)
 
 
+def test_small_batch_decode_with_normalising_projections_matches_the_separate_layernorms() -> None:
+    """3 sequences: LayerNorms inside the projections (the default for at most 8) give the same tokens, bit for bit
+    the same computation, as separate LayerNorm launches; both match the oracle."""
+    from tempo_compiler_b200.engine import Engine
+    from tempo_compiler_b200.weights import random_gpt2, random_token_ids
+    layers, shared = random_gpt2(61)
+    batch, prompt, steps = 3, 48, 10
+    ids = np.stack([random_token_ids(500 + s, prompt) for s in range(batch)]).astype(np.int32)
+    fused = Engine(layers, shared, batch=batch, prompt=prompt, capacity=prompt + steps)
+    assert fused.fuse_small_norms
+    tokens = fused.generate(ids, steps)
+    separate = Engine(layers, shared, batch=batch, prompt=prompt, capacity=prompt + steps, fuse_small_norms=False)
+    np.testing.assert_array_equal(separate.generate(ids, steps), tokens)
+    for s in range(batch):
+        _check_teacher_forced(layers, shared, ids[s], tokens[s])
+
+
 def test_free_running_greedy_identity_on_a_short_decode() -> None:
     from tempo_compiler_b200.engine import Engine
     from tempo_compiler_b200.weights import random_gpt2, random_token_ids

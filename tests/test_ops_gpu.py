@@ -209,6 +209,50 @@ def test_gemm_gelu_on_every_bf16_input(m_extra: int) -> None:
     assert (steps > 0).sum().item() <= 16, (steps > 0).sum().item()
 
 
+@pytest.mark.parametrize("m", [1, 3, 8])
+def test_gemm_norm_has_the_bits_of_layernorm_then_gemm(m: int) -> None:
+    """tempo_gemm_norm against tempo_layernorm followed by the same projection: QKV with the cache store, FC with
+    GELU, and the LM head's argmax partials -- identical outputs, caches and partials."""
+    from tempo_compiler_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(m + 100)
+    x = (torch.randn((m, 768), generator=g, device="cuda") * 3 + 0.5).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(768, generator=g, device="cuda")).to(torch.bfloat16)
+    beta = (0.1 * torch.randn(768, generator=g, device="cuda")).to(torch.bfloat16)
+    ln = ops.layernorm(x, gamma, beta, epsilon=1e-5)
+    # QKV + bias + cache store at positions
+    w = (torch.randn((2304, 768), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    b = (torch.randn(2304, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    positions = torch.arange(m, dtype=torch.int32, device="cuda") * 5 + 3
+    caches = [torch.zeros((m, 12, 64, 64), dtype=torch.bfloat16, device="cuda") for _ in range(4)]
+    want = torch.empty((m, 2304), dtype=torch.bfloat16, device="cuda")
+    ops.gemm_qkv(ln, w, b, want, caches[0], caches[1], positions=positions)
+    got = ops.gemm_norm(x, gamma, beta, w, epsilon=1e-5, bias=b, k_cache=caches[2], v_cache=caches[3],
+                        positions=positions)
+    assert torch.equal(got, want)
+    assert torch.equal(caches[2], caches[0]) and torch.equal(caches[3], caches[1])
+    assert caches[2].abs().sum() > 0
+    # FC + bias + GELU
+    w = (torch.randn((3072, 768), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    b = (torch.randn(3072, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    assert torch.equal(ops.gemm_norm(x, gamma, beta, w, epsilon=1e-5, bias=b, gelu=True),
+                       ops.gemm(ln, w, bias=b, gelu=True))
+    # LM head argmax partials
+    wte = (torch.randn((50257, 768), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    tiles = (50257 + 255) // 256
+    parts = [torch.empty((m, tiles), dtype=dt, device="cuda") for dt in (torch.float32, torch.int32) * 2]
+    ops.gemm_argmax(ln, wte, parts[0], parts[1])
+    ops.gemm_norm(x, gamma, beta, wte, epsilon=1e-5, part_val=parts[2], part_idx=parts[3])
+    assert torch.equal(parts[0], parts[2]) and torch.equal(parts[1], parts[3])
+
+
+def test_gemm_norm_refuses_more_than_8_rows() -> None:
+    from tempo_compiler_b200 import ops
+    x = torch.zeros((9, 768), dtype=torch.bfloat16, device="cuda")
+    ones = torch.ones(768, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError):
+        ops.gemm_norm(x, ones, ones, torch.zeros((64, 768), dtype=torch.bfloat16, device="cuda"))
+
+
 def test_stream_read_folds_every_word() -> None:
     """The calibration read touches every word of a source of whole groups: the XOR of its sink words is the XOR of
     all source words."""
