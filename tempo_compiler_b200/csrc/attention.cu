@@ -301,11 +301,12 @@ extern "C" tempo_status tempo_decode_attention(const void* qkv, const void* k_ca
   if (!aligned16(qkv) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
     return fail(TEMPO_ERR_VALUE, "tempo_decode_attention: operands must be 16-byte aligned");
   // Fewer (sequence, head) pairs than SMs (a handful of sequences): split each over up to eight CTAs of a cluster,
-  // each with at least 128 keys of the capacity, until every SM has one. Larger batches keep one CTA per pair: the
-  // cluster merge costs more than the parallelism it adds once every SM is busy.
+  // each with at least 64 keys of the capacity (one iteration of the 4-key variant's four warps), until every SM has
+  // one. Larger batches keep one CTA per pair: the cluster merge costs more than the parallelism it adds once every
+  // SM is busy.
   const uint64_t pairs = uint64_t(seqs) * heads, target = uint64_t(sm_count());
   uint32_t chunks = 1;
-  while (chunks < kDecodeMaxChunks && pairs * chunks < target && capacity >= 2 * 128 * chunks) chunks *= 2;
+  while (chunks < kDecodeMaxChunks && pairs * chunks < target && capacity >= 2 * 64 * chunks) chunks *= 2;
   // A grid that fits at eight CTAs per SM runs the 4-key variant, entirely resident; larger grids the 8-key one.
   const uint64_t ctas = pairs * chunks;
   const bool small = single_wave(ctas, 8) != 0;

@@ -13,7 +13,6 @@ namespace tempo {
 namespace {
 
 constexpr int kWarps = 8;
-constexpr int kCols = 2;               // output columns a warp carries at once
 constexpr uint32_t kArgmaxTile = 256;  // columns one argmax partial covers (matches the tensor-core path)
 
 struct GemvParams {
@@ -39,46 +38,60 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
-// Dot products of kCols weight rows with every activation row: acc[c][r] summed over the whole warp.
-template <int M>
+// Dot products of CP weight rows (columns n0 .. n0 + CP - 1) with every activation row, summed over the warp into
+// acc[c][r]. Lane l covers the 16-byte chunks l, l + 32, ... of the contraction; each pass first issues all of its
+// CP x KCH weight loads, then does the arithmetic, so a lane keeps up to CP x KCH loads in flight (the memory-level
+// parallelism the HBM needs at a handful of rows), and passes repeat while chunks remain.
+template <int M, int KCH, int CP>
 __device__ __forceinline__ void dot_columns(const GemvParams& p, const uint16_t* a_smem, uint32_t n0,
-                                            float (&acc)[kCols][M]) {
+                                            float (&acc)[CP][M]) {
   const uint32_t lane = lane_id();
 #pragma unroll
-  for (int c = 0; c < kCols; ++c)
+  for (int c = 0; c < CP; ++c)
 #pragma unroll
     for (int r = 0; r < M; ++r) acc[c][r] = 0.f;
   const uint32_t chunks = p.k / 8;
-#pragma unroll 2
-  for (uint32_t ch = lane; ch < chunks; ch += 32) {
-    uint4 wv[kCols];
+  for (uint32_t base = 0; base < chunks; base += 32 * KCH) {
+    uint4 wv[CP][KCH];
 #pragma unroll
-    for (int c = 0; c < kCols; ++c)
-      wv[c] = n0 + c < p.n ? __ldg(reinterpret_cast<const uint4*>(p.w + size_t(n0 + c) * p.ldw) + ch)
-                           : make_uint4(0, 0, 0, 0);
+    for (int c = 0; c < CP; ++c) {
+      const uint4* row = reinterpret_cast<const uint4*>(p.w + size_t(n0 + c) * p.ldw);
 #pragma unroll
-    for (int r = 0; r < M; ++r) {
-      if (r >= int(p.m)) break;
-      float av[8];
-      unpack8(*reinterpret_cast<const uint4*>(a_smem + size_t(r) * p.k + ch * 8), av);
+      for (int i = 0; i < KCH; ++i) {
+        const uint32_t ch = base + lane + 32u * i;
+        wv[c][i] = (n0 + c < p.n && ch < chunks) ? __ldg(row + ch) : make_uint4(0, 0, 0, 0);
+      }
+    }
 #pragma unroll
-      for (int c = 0; c < kCols; ++c) {
-        float wf[8];
-        unpack8(wv[c], wf);
+    for (int i = 0; i < KCH; ++i) {
+      const uint32_t ch = base + lane + 32u * i;
+      if (ch >= chunks) break;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[c][r] = fmaf(av[j], wf[j], acc[c][r]);
+      for (int r = 0; r < M; ++r) {
+        if (r >= int(p.m)) break;
+        float av[8];
+        unpack8(*reinterpret_cast<const uint4*>(a_smem + size_t(r) * p.k + ch * 8), av);
+#pragma unroll
+        for (int c = 0; c < CP; ++c) {
+          float wf[8];
+          unpack8(wv[c][i], wf);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[c][r] = fmaf(av[j], wf[j], acc[c][r]);
+        }
       }
     }
   }
 #pragma unroll
-  for (int c = 0; c < kCols; ++c)
+  for (int c = 0; c < CP; ++c)
 #pragma unroll
     for (int r = 0; r < M; ++r)
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) acc[c][r] += __shfl_xor_sync(0xFFFFFFFFu, acc[c][r], o);
 }
 
-template <int M>
+// One warp per output column (CP = 1), or, in argmax mode, 32 columns of the block's 256-column tile per warp taken
+// CP at a time.
+template <int M, int KCH, int CP>
 __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(GemvParams p) {
   extern __shared__ __align__(16) uint16_t a_smem[];
   __shared__ float best_val[kWarps][M];
@@ -86,16 +99,14 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(GemvParams p) {
   const uint32_t warp = warp_id(), lane = lane_id();
   const bool argmax = (p.flags & TEMPO_GEMM_ARGMAX) != 0;
   const bool gelu = (p.flags & TEMPO_GEMM_GELU) != 0;
-  // Argmax: a block covers one 256-column tile (32 columns per warp). Otherwise a warp covers kCols columns.
-  const uint32_t warp_cols = argmax ? kArgmaxTile / kWarps : kCols;
+  const uint32_t warp_cols = argmax ? kArgmaxTile / kWarps : uint32_t(CP);
   const uint32_t first = (blockIdx.x * kWarps + warp) * warp_cols;
 
   // The weights are not the previous kernel's output: start pulling this warp's rows into L2 now.
-  for (uint32_t c = 0; c < warp_cols; c += kCols)
-    for (uint32_t cc = 0; cc < kCols; ++cc)
-      if (first + c + cc < p.n)
-        for (uint32_t line = lane; line < p.k * 2 / 128; line += 32)
-          prefetch_l2(reinterpret_cast<const uint8_t*>(p.w + size_t(first + c + cc) * p.ldw) + line * 128);
+  for (uint32_t c = 0; c < warp_cols; ++c)
+    if (first + c < p.n)
+      for (uint32_t line = lane; line < p.k * 2 / 128; line += 32)
+        prefetch_l2(reinterpret_cast<const uint8_t*>(p.w + size_t(first + c) * p.ldw) + line * 128);
   pdl_launch_dependents();
   pdl_wait();
 
@@ -117,14 +128,14 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(GemvParams p) {
 #pragma unroll
   for (int r = 0; r < M; ++r) { best[r] = -INFINITY; idx[r] = 0; }
 
-  for (uint32_t c0 = 0; c0 < warp_cols; c0 += kCols) {
+  for (uint32_t c0 = 0; c0 < warp_cols; c0 += CP) {
     const uint32_t n0 = first + c0;
     if (n0 >= p.n) break;
-    float acc[kCols][M];
-    dot_columns<M>(p, a_smem, n0, acc);
+    float acc[CP][M];
+    dot_columns<M, KCH, CP>(p, a_smem, n0, acc);
     if (argmax) {
 #pragma unroll
-      for (int c = 0; c < kCols; ++c)
+      for (int c = 0; c < CP; ++c)
 #pragma unroll
         for (int r = 0; r < M; ++r)
           if (n0 + c < p.n && acc[c][r] > best[r]) { best[r] = acc[c][r]; idx[r] = int32_t(n0 + c); }
@@ -132,7 +143,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(GemvParams p) {
     }
     // Lane (c * M + r) finishes column n0 + c of row r.
 #pragma unroll
-    for (int c = 0; c < kCols; ++c) {
+    for (int c = 0; c < CP; ++c) {
 #pragma unroll
       for (int r = 0; r < M; ++r) {
         if (lane != uint32_t(c * M + r) || r >= int(p.m) || n0 + c >= p.n) continue;
@@ -167,15 +178,31 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(GemvParams p) {
   }
 }
 
+template <int M, int KCH, int CP>
+tempo_status launch_gemv_shape(const GemvParams& p, cudaStream_t stream) {
+  const bool argmax = (p.flags & TEMPO_GEMM_ARGMAX) != 0;
+  const uint32_t cols_per_block = argmax ? kArgmaxTile : kWarps * CP;
+  const uint32_t blocks = (p.n + cols_per_block - 1) / cols_per_block;
+  const size_t smem = size_t(p.m) * p.k * 2;
+  tempo_status s = set_smem(reinterpret_cast<const void*>(gemv_kernel<M, KCH, CP>), 96 * 1024);
+  if (s != TEMPO_OK) return s;
+  return launch(gemv_kernel<M, KCH, CP>, dim3(blocks), dim3(kWarps * 32), smem, stream, 1, "gemv_kernel", p);
+}
+
+// Chunks per lane and pass: the whole contraction for K <= 768 (3) and K <= 3072 (12, one column at a time), else
+// passes of 4. The argmax tile's 32 columns per warp go several at a time.
 template <int M>
 tempo_status launch_gemv(const GemvParams& p, cudaStream_t stream) {
   const bool argmax = (p.flags & TEMPO_GEMM_ARGMAX) != 0;
-  const uint32_t cols_per_block = argmax ? kArgmaxTile : kWarps * kCols;
-  const uint32_t blocks = (p.n + cols_per_block - 1) / cols_per_block;
-  const size_t smem = size_t(p.m) * p.k * 2;
-  tempo_status s = set_smem(reinterpret_cast<const void*>(gemv_kernel<M>), 96 * 1024);
-  if (s != TEMPO_OK) return s;
-  return launch(gemv_kernel<M>, dim3(blocks), dim3(kWarps * 32), smem, stream, 1, "gemv_kernel", p);
+  const uint32_t per_lane = (p.k / 8 + 31) / 32;
+  if (argmax) {
+    // four columns at a time for one or two rows; two for more, which keeps two CTAs resident per SM
+    if (per_lane <= 3) return launch_gemv_shape<M, 3, (M <= 2 ? 4 : 2)>(p, stream);
+    return launch_gemv_shape<M, 4, 2>(p, stream);
+  }
+  if (per_lane <= 3) return launch_gemv_shape<M, 3, 1>(p, stream);
+  if (per_lane <= 12 && per_lane > 4) return launch_gemv_shape<M, 12, 1>(p, stream);
+  return launch_gemv_shape<M, 4, 1>(p, stream);
 }
 
 }  // namespace

@@ -545,6 +545,8 @@ def _fused_packed_cache(cache: np.ndarray) -> np.ndarray:
     (2, 1152, (1024, 1100)),            # eight CTAs per (sequence, head), the last one's key range empty
     (4, 512, (0, 1, 200, 512)),         # four per pair: empty, single-key and ragged lengths
     (90, 256, tuple(range(1, 91))),     # two per pair, every length 1..90
+    (1, 383, (129,)),                   # four per pair of 64-key chunks, the last two empty
+    (2, 383, (383, 200)),               # four per pair, a full and a ragged cache
 ])
 def test_native_decode_attention_matches_fp32(seqs: int, capacity: int, lengths) -> None:
     from tempo_compiler_b200 import ops
