@@ -410,14 +410,24 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
   return w;
 }
 
+// The LayerNorm's per-element steps, written out (explicit fused multiply-adds) so that every kernel normalising a
+// row rounds exactly alike: the centred square accumulated, and (x - mean) rstd gamma + beta.
+__device__ __forceinline__ float ln_square_add(float x, float mean, float acc) {
+  const float d = x - mean;
+  return fmaf(d, d, acc);
+}
+__device__ __forceinline__ float ln_apply(float x, float mean, float scale, float gamma, float beta) {
+  return fmaf((x - mean) * scale, gamma, beta);
+}
+
 // One row's LayerNorm by one warp: lane l holds the row's 16-byte chunks l, l + 32, ... (up to CPL of them, `features`
-// / 8 in all); mean, centred variance, rsqrt(var + epsilon), then (x - mean) rstd gamma + beta rounded to BF16 into
-// `orow` (global or shared memory). The standalone LayerNorm and the small-M projections that normalise their own
+// / 8 in all); mean, centred variance, rsqrt(var + epsilon), then (x - mean) rstd gamma + beta rounded to BF16, chunk
+// c handed to store(c, word) (layernorm_row: into `orow`, global or shared memory). The standalone LayerNorm and the small-M projections that normalise their own
 // input share it, so both produce the same bits; a larger CPL than needed only skips chunks, in the same order.
-template <int CPL>
-__device__ __forceinline__ void layernorm_row(const uint16_t* __restrict__ xr, const uint16_t* __restrict__ gamma,
-                                              const uint16_t* __restrict__ beta, uint32_t features, float epsilon,
-                                              uint16_t* orow) {
+template <int CPL, typename Store>
+__device__ __forceinline__ void layernorm_row_to(const uint16_t* __restrict__ xr, const uint16_t* __restrict__ gamma,
+                                                 const uint16_t* __restrict__ beta, uint32_t features, float epsilon,
+                                                 Store store) {
   const uint32_t lane = lane_id();
   const uint32_t chunks = features / 8;
   float v[CPL][8];
@@ -438,7 +448,7 @@ __device__ __forceinline__ void layernorm_row(const uint16_t* __restrict__ xr, c
   for (int i = 0; i < CPL; ++i) {
     if (lane + 32u * i < chunks) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) sq += (v[i][j] - mean) * (v[i][j] - mean);
+      for (int j = 0; j < 8; ++j) sq = ln_square_add(v[i][j], mean, sq);
     }
   }
   const float scale = rsqrtf(warp_sum(sq) * inv_f + epsilon);
@@ -450,10 +460,18 @@ __device__ __forceinline__ void layernorm_row(const uint16_t* __restrict__ xr, c
       unpack8(__ldg(reinterpret_cast<const uint4*>(gamma + c * 8)), g);
       unpack8(__ldg(reinterpret_cast<const uint4*>(beta + c * 8)), b);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[i][j] = (v[i][j] - mean) * scale * g[j] + b[j];
-      *reinterpret_cast<uint4*>(orow + c * 8) = pack8(v[i]);
+      for (int j = 0; j < 8; ++j) v[i][j] = ln_apply(v[i][j], mean, scale, g[j], b[j]);
+      store(c, pack8(v[i]));
     }
   }
+}
+
+template <int CPL>
+__device__ __forceinline__ void layernorm_row(const uint16_t* __restrict__ xr, const uint16_t* __restrict__ gamma,
+                                              const uint16_t* __restrict__ beta, uint32_t features, float epsilon,
+                                              uint16_t* orow) {
+  layernorm_row_to<CPL>(xr, gamma, beta, features, epsilon,
+                        [orow](uint32_t c, const uint4& w) { *reinterpret_cast<uint4*>(orow + c * 8) = w; });
 }
 
 __device__ __forceinline__ bool elect_one() {
