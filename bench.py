@@ -198,25 +198,31 @@ class Clocks:
             self.proc.kill()
         if self.thread is not None:
             self.thread.join(timeout=2)
+        return self.summarize(self.lines, self.t_start, self.t_end, len(self.indices))
+
+    @classmethod
+    def summarize(cls, lines: list[str], t_start: float, t_end: float, gpus: int) -> dict | None:
+        """Median SM clock, maximum clock and the throttle reasons of the samples stamped inside [t_start, t_end]
+        (50 ms of slack either side); with none inside (a region shorter than the interval), the first sample of
+        each GPU after t_start."""
         rows = []
-        for line in self.lines:
+        for line in lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 10:
                 continue
-            stamp = self._stamp(parts[0])
+            stamp = cls._stamp(parts[0])
             try:
                 rows.append((stamp, float(parts[2]), float(parts[3]), parts[6:10]))
             except ValueError:
                 continue
-        inside = [r for r in rows if r[0] is not None and self.t_start - 0.05 <= r[0] <= self.t_end + 0.05]
-        used = inside or [r for r in rows if r[0] is not None and r[0] >= self.t_start][:len(self.indices)]
+        inside = [r for r in rows if r[0] is not None and t_start - 0.05 <= r[0] <= t_end + 0.05]
+        used = inside or [r for r in rows if r[0] is not None and r[0] >= t_start][:gpus]
         if not used:
             return None
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = {name for r in used for name, value in zip(names, r[3]) if value.lower() == "active"}
         return {"sm_mhz": statistics.median(r[1] for r in used), "sm_max_mhz": max(r[2] for r in used),
-                "reasons": sorted(reasons), "samples": len(used), "gpus": len(self.indices),
-                "in_timed_region": bool(inside)}
+                "reasons": sorted(reasons), "samples": len(used), "gpus": gpus, "in_timed_region": bool(inside)}
 
 
 def _job_gpu_indices(world: int) -> list[int]:

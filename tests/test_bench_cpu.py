@@ -1,0 +1,47 @@
+"""bench.py's host-side pieces that need no GPU: the clock-sample window and the job's GPU indices."""
+
+from __future__ import annotations
+
+import datetime
+
+import bench
+
+
+def _line(when: float, index: int, mhz: float, power_cap: bool = False, thermal: bool = False) -> str:
+    stamp = datetime.datetime.fromtimestamp(when).strftime("%Y/%m/%d %H:%M:%S.%f")[:-3]
+    active = "Active" if power_cap else "Not Active"
+    hot = "Active" if thermal else "Not Active"
+    return f"{stamp}, {index}, {mhz}, 1965, 900.00, 0x0000000000000000, Not Active, {hot}, Not Active, {active}"
+
+
+def test_only_samples_inside_the_timed_region_count() -> None:
+    t0 = 1_000_000.0
+    lines = [_line(t0 - 1.0, 0, 300.0, thermal=True),      # idle, before the region
+             _line(t0 + 0.1, 0, 1800.0, power_cap=True),
+             _line(t0 + 0.2, 0, 1900.0),
+             _line(t0 + 0.3, 0, 1850.0),
+             _line(t0 + 2.0, 0, 400.0)]                    # after the region
+    summary = bench.Clocks.summarize(lines, t0, t0 + 0.35, 1)
+    assert summary["samples"] == 3 and summary["in_timed_region"]
+    assert summary["sm_mhz"] == 1850.0 and summary["sm_max_mhz"] == 1965.0
+    assert summary["reasons"] == ["sw_power_cap"]
+
+
+def test_a_region_shorter_than_the_interval_takes_the_next_sample_of_each_gpu() -> None:
+    t0 = 2_000_000.0
+    lines = [_line(t0 + 0.5, 0, 1700.0), _line(t0 + 0.5, 1, 1750.0), _line(t0 + 0.6, 0, 1000.0)]
+    summary = bench.Clocks.summarize(lines, t0, t0 + 0.01, 2)
+    assert summary["samples"] == 2 and not summary["in_timed_region"]
+    assert summary["sm_mhz"] == 1725.0 and summary["gpus"] == 2
+
+
+def test_no_samples_gives_no_clock_record() -> None:
+    assert bench.Clocks.summarize([], 0.0, 1.0, 1) is None
+    assert bench.Clocks.summarize(["garbage"], 0.0, 1.0, 1) is None
+
+
+def test_job_gpus_follow_the_visible_devices(monkeypatch) -> None:
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES", raising=False)
+    assert bench._job_gpu_indices(4) == [0, 1, 2, 3]
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "4,5,6,7")
+    assert bench._job_gpu_indices(2) == [4, 5]
