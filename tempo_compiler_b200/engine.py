@@ -13,6 +13,8 @@ is the B200 layout of the same math:
   input) and the residual add are fused into the GEMM epilogue, so the add images vanish;
 * keys and values are stored once per token into a [seq][head][position][64] cache, which decode attention streams;
 * the LM head's argmax is fused into its GEMM epilogue, so the 50257-wide logits never reach HBM;
+* with at most 8 sequences per decode group each LayerNorm runs inside the projection after it (``gemm_norm``, the
+  same bits as the separate kernels), two launches fewer per layer;
 * the decode step (embedding, 12 layers, LM head, argmax, position advance) is captured once as a CUDA graph and
   replayed, its varying state (ids, positions) living in device buffers.
 
