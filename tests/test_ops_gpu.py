@@ -500,7 +500,9 @@ def test_block_causal_attention_within_two_percent(tokens: int) -> None:
         assert error < 0.02, (h, error)
 
 
-@pytest.mark.parametrize(("seqs", "tokens"), [(1, 64), (2, 200), (3, 128), (1, 1024), (4, 384)])
+@pytest.mark.parametrize(("seqs", "tokens"), [(1, 64), (2, 200), (3, 128), (1, 1024), (4, 384),
+                                             (4, 1024),    # 384 (query tile, head, sequence) items: more than two per SM
+                                             (24, 1000)])  # 2304 items over several waves, a ragged last query tile
 def test_native_prefill_attention_matches_fp32(seqs: int, tokens: int) -> None:
     from tempo_compiler_b200 import ops
     g = torch.Generator(device="cuda").manual_seed(seqs * 1000 + tokens)
