@@ -1,5 +1,5 @@
-// Causal prefill attention on the 5th-generation tensor cores (flash-attention tile loop, one CTA per 128 queries of
-// one head of one sequence, two CTAs per SM).
+// Causal prefill attention on the 5th-generation tensor cores (flash-attention tile loop over 128 queries of one head
+// of one sequence at a time; persistent CTAs, two per SM, each walking a share of those items).
 //
 //   warp 0      TMA: Q once, then K and V 64 keys at a time into a four-stage ring.
 //   warp 1      MMA issuer and TMEM owner. S = Q K^T goes into one of two 64-column TMEM buffers (FP32), so the
@@ -48,13 +48,13 @@ struct PrefillParams {
   uint32_t early;        // the grid fits in one wave: dependents may launch at entry
 };
 
-// Shared memory: Q | K[kStages] | V[kStages] | barriers.
+// Shared memory: Q[2] (the current and the next item's) | K[kStages] | V[kStages] | barriers.
 constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kQBytes;
+constexpr uint32_t kOffK = 2 * kQBytes;
 constexpr uint32_t kOffV = kOffK + kStages * kKvTileBytes;
 constexpr uint32_t kOffBar = kOffV + kStages * kKvTileBytes;
-// q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full, final
-constexpr uint32_t kBarCount = 1 + 2 * kStages + 2 + 2 + 1 + 1;
+// q_full[2], kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full, final, q_empty[2], o_done
+constexpr uint32_t kBarCount = 2 + 2 * kStages + 2 + 2 + 1 + 1 + 2 + 1;
 constexpr uint32_t kSmem = kOffBar + kBarCount * 8 + 16 + 1024;
 
 // TMEM columns: S/P buffer 0 | S/P buffer 1 | O.
@@ -84,6 +84,30 @@ __device__ __forceinline__ uint64_t v_desc(uint32_t tile_addr, uint32_t kk) {
   else return make_smem_desc(tile_addr + kk * 2048, 8192, 1024, kLayoutSw128);
 }
 
+// One (query tile, head, sequence) of the grid's work. The CTAs are persistent (at most kCtasPerSm per SM, all
+// resident at once): the items are ranked heaviest first (causal: query tile qt reads about 2(qt + 1) key tiles) and
+// dealt to the CTAs in snake order (round k hands out ranks kG .. kG + G - 1, ascending in even rounds and
+// descending in odd ones), which evens out the key tiles per CTA. A CTA's TMA, MMA and softmax roles walk the same
+// sequence, so one item's Q and first keys load while the previous item's last tiles and output are finished.
+struct PrefillItem {
+  uint32_t qt, h, s, kv_tiles, first_masked;
+};
+
+__device__ __forceinline__ bool next_item(const PrefillParams& p, uint32_t k, PrefillItem& it) {
+  const uint32_t grid = gridDim.x, cta = blockIdx.x;
+  const uint64_t rank = uint64_t(k) * grid + ((k & 1u) ? grid - 1 - cta : cta);
+  const uint32_t per_tile = p.heads * p.seqs;
+  if (rank >= uint64_t(p.q_tiles) * per_tile) return false;
+  const uint32_t r = uint32_t(rank), rem = r % per_tile;
+  it.qt = p.q_tiles - 1 - r / per_tile;
+  it.h = rem % p.heads;
+  it.s = rem / p.heads;
+  const uint32_t last_query = min(p.tokens, (it.qt + 1) * 128) - 1;
+  it.kv_tiles = last_query / kKeys + 1;
+  it.first_masked = (it.qt * 128) / kKeys;  // key tiles from here on reach past the tile's first query
+  return true;
+}
+
 template <bool PACKED>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     attention_prefill_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_kv,
@@ -92,27 +116,25 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 1 + kStages;
-  uint64_t* s_full = bars + 1 + 2 * kStages;
+  uint64_t* kv_full = bars + 2;
+  uint64_t* kv_empty = bars + 2 + kStages;
+  uint64_t* s_full = bars + 2 + 2 * kStages;
   uint64_t* p_full = s_full + 2;
   uint64_t* o_full = p_full + 2;
   uint64_t* final_bar = o_full + 1;
+  uint64_t* q_empty = final_bar + 1;  // [2]
+  uint64_t* o_done = q_empty + 2;     // completes once per item, after its last P V
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBarCount);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  // Heaviest query tiles first (causal: tile qt reads about 2(qt+1) key tiles).
-  const uint32_t qt = p.q_tiles - 1 - (blockIdx.x % p.q_tiles);
-  const uint32_t h = (blockIdx.x / p.q_tiles) % p.heads;
-  const uint32_t s = blockIdx.x / (p.q_tiles * p.heads);
-  const uint32_t last_query = min(p.tokens, (qt + 1) * 128) - 1;
-  const uint32_t kv_tiles = last_query / kKeys + 1;
-  const uint32_t first_masked = (qt * 128) / kKeys;  // key tiles from here on reach past the tile's first query
   const uint32_t warp = warp_id(), lane = lane_id();
   const uint32_t heads4 = p.heads * 4;  // 16-wide feature tiles per third of the fused tensor
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
     for (uint32_t i = 0; i < kStages; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
@@ -123,6 +145,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
     mbar_init(o_full, 1);
     mbar_init(final_bar, 1);
+    mbar_init(o_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmap_q);
@@ -139,13 +162,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   if (p.early) pdl_launch_dependents();
   pdl_wait();  // Q, K and V are the previous kernel's output
 
-  auto q_coord = [&]() -> int32_t {
-    if constexpr (PACKED) return int32_t(qt * 4);
-    else return int32_t(s * p.tokens + qt * 128);
+  auto q_coord = [&](const PrefillItem& it) -> int32_t {
+    if constexpr (PACKED) return int32_t(it.qt * 4);
+    else return int32_t(it.s * p.tokens + it.qt * 128);
   };
-  auto kv_coord = [&](uint32_t j) -> int32_t {
+  auto kv_coord = [&](const PrefillItem& it, uint32_t j) -> int32_t {
     if constexpr (PACKED) return int32_t(j * (kKeys / 32));
-    else return int32_t(s * p.tokens + j * kKeys);
+    else return int32_t(it.s * p.tokens + j * kKeys);
   };
 
   if (warp == 0) {
@@ -153,18 +176,31 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       bool issued[kStages];
       uint32_t parity_of[kStages];
       for (uint32_t i = 0; i < kStages; ++i) { issued[i] = false; parity_of[i] = 0; }
-      mbar_arrive_expect_tx(q_full, kQBytes);
-      load_tile<PACKED>(smem + kOffQ, &tmap_q, q_full, h * 4, q_coord());
-      for (uint32_t j = 0; j < kv_tiles; ++j) {
-        const uint32_t st = j % kStages, ph = (j / kStages) & 1u;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1u, kWatchEmpty, abort_flag)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kKvTileBytes);
-        load_tile<PACKED>(smem + kOffK + st * kKvTileBytes, &tmap_kv, &kv_full[st], heads4 + h * 4, kv_coord(j));
-        load_tile<PACKED>(smem + kOffV + st * kKvTileBytes, &tmap_kv, &kv_full[st], 2 * heads4 + h * 4, kv_coord(j));
-        issued[st] = true;
-        parity_of[st] = ph;
+      uint32_t g = 0, items = 0;  // key tiles and items this CTA has loaded
+      bool ok = true;
+      PrefillItem it;
+      for (uint32_t k = 0; ok && next_item(p, k, it); ++k) {
+        // Item k's Q buffer (k & 1) is free once every S of item k - 2 has completed.
+        const uint32_t qb = k & 1u;
+        if (!mbar_wait(&q_empty[qb], ((k >> 1) & 1u) ^ 1u, kWatchEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(&q_full[qb], kQBytes);
+        load_tile<PACKED>(smem + kOffQ + qb * kQBytes, &tmap_q, &q_full[qb], it.h * 4, q_coord(it));
+        ++items;
+        for (uint32_t j = 0; j < it.kv_tiles; ++j, ++g) {
+          const uint32_t st = g % kStages, ph = (g / kStages) & 1u;
+          if (!mbar_wait(&kv_empty[st], ph ^ 1u, kWatchEmpty, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&kv_full[st], 2 * kKvTileBytes);
+          load_tile<PACKED>(smem + kOffK + st * kKvTileBytes, &tmap_kv, &kv_full[st], heads4 + it.h * 4,
+                            kv_coord(it, j));
+          load_tile<PACKED>(smem + kOffV + st * kKvTileBytes, &tmap_kv, &kv_full[st], 2 * heads4 + it.h * 4,
+                            kv_coord(it, j));
+          issued[st] = true;
+          parity_of[st] = ph;
+        }
       }
-      mbar_wait(q_full, 0, kWatchFull, nullptr);
+      // Every copy issued must have landed before the CTA may exit.
+      for (uint32_t k = items > 2 ? items - 2 : 0; k < items; ++k)
+        mbar_wait(&q_full[k & 1u], (k >> 1) & 1u, kWatchFull, nullptr);
       for (uint32_t i = 0; i < kStages; ++i)
         if (issued[i]) mbar_wait(&kv_full[i], parity_of[i], kWatchFull, nullptr);
     }
@@ -172,33 +208,51 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     if (elect_one()) {
       constexpr uint32_t idesc_s = make_idesc_bf16(128, kKeys, 0, 0);
       constexpr uint32_t idesc_o = make_idesc_bf16(128, 64, 0, 1);
-      const uint32_t q_addr = smem_u32(smem + kOffQ);
-      // S_j = Q K_j^T into buffer j & 1. The buffer held P_{j-2}, whose P V was issued before (issue order).
-      auto issue_s = [&](uint32_t j) -> bool {
-        const uint32_t st = j % kStages;
-        if (!mbar_wait(&kv_full[st], (j / kStages) & 1u, kWatchFull, abort_flag)) return false;
+      uint32_t q_addr = smem_u32(smem + kOffQ);
+      // S_g = Q K_g^T (g counts this CTA's key tiles over all its items) into buffer g & 1. The buffer held
+      // P_{g-2}, whose P V was issued before (the MMAs of one thread run in issue order).
+      auto issue_s = [&](uint32_t g) -> bool {
+        const uint32_t st = g % kStages;
+        if (!mbar_wait(&kv_full[st], (g / kStages) & 1u, kWatchFull, abort_flag)) return false;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(smem + kOffK + st * kKvTileBytes);
-        const uint32_t d = tmem_base + ((j & 1u) ? kTmemS1 : kTmemS0);
+        const uint32_t d = tmem_base + ((g & 1u) ? kTmemS1 : kTmemS0);
 #pragma unroll
         for (uint32_t kk = 0; kk < 4; ++kk)
           umma_bf16(d, kmajor_desc<PACKED>(q_addr, kk, 128), kmajor_desc<PACKED>(k_addr, kk, kKeys), idesc_s,
                     kk != 0);
-        umma_commit(&s_full[j & 1u]);
+        umma_commit(&s_full[g & 1u]);
         return true;
       };
-      bool ok = mbar_wait(q_full, 0, kWatchFull, abort_flag) && issue_s(0);
-      for (uint32_t j = 0; j < kv_tiles && ok; ++j) {
-        if (j + 1 < kv_tiles && !issue_s(j + 1)) break;
-        if (!mbar_wait(&p_full[j & 1u], (j >> 1) & 1u, kWatchOther, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(smem + kOffV + (j % kStages) * kKvTileBytes);
-        const uint32_t pa = tmem_base + ((j & 1u) ? kTmemS1 : kTmemS0);
+      uint32_t g = 0;
+      bool ok = true;
+      PrefillItem it;
+      for (uint32_t k = 0; ok && next_item(p, k, it); ++k) {
+        q_addr = smem_u32(smem + kOffQ + (k & 1u) * kQBytes);
+        ok = mbar_wait(&q_full[k & 1u], (k >> 1) & 1u, kWatchFull, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          ok = issue_s(g);
+        }
+        for (uint32_t j = 0; j < it.kv_tiles && ok; ++j, ++g) {
+          if (j + 1 < it.kv_tiles) {
+            if (!issue_s(g + 1)) { ok = false; break; }
+          } else {
+            umma_commit(&q_empty[k & 1u]);  // every S of this item is issued: its Q is free once they complete
+          }
+          // The item's first P V overwrites O: the softmax threads read the previous item's O before they
+          // signalled this P.
+          if (!mbar_wait(&p_full[g & 1u], (g >> 1) & 1u, kWatchOther, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(smem + kOffV + (g % kStages) * kKvTileBytes);
+          const uint32_t pa = tmem_base + ((g & 1u) ? kTmemS1 : kTmemS0);
 #pragma unroll
-        for (uint32_t kk = 0; kk < kKeys / 16; ++kk)
-          umma_bf16_tmem_a(tmem_base + kTmemO, pa + kk * 8, v_desc<PACKED>(v_addr, kk), idesc_o, (j | kk) != 0u);
-        umma_commit(o_full);
-        umma_commit(&kv_empty[j % kStages]);
+          for (uint32_t kk = 0; kk < kKeys / 16; ++kk)
+            umma_bf16_tmem_a(tmem_base + kTmemO, pa + kk * 8, v_desc<PACKED>(v_addr, kk), idesc_o, (j | kk) != 0u);
+          umma_commit(o_full);
+          if (j + 1 == it.kv_tiles) umma_commit(o_done);
+          umma_commit(&kv_empty[g % kStages]);
+        }
       }
       umma_commit(final_bar);
       mbar_wait(final_bar, 0, kWatchOther, nullptr);
@@ -206,130 +260,133 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   } else {
     const uint32_t lane_base = 32u * (warp & 3u);
     const uint32_t row = lane_base + lane;
-    const uint32_t q_local = qt * 128 + row;  // query position in the sequence
     const uint32_t lane_addr = lane_base << 16;
     const uint32_t tmem_o = tmem_base + kTmemO;
-    float m_used = -INFINITY, l = 0.f;  // m_used: raw-score units
+    uint32_t g = 0;  // this CTA's key tiles so far, over all its items
     bool ok = true;
-    for (uint32_t j = 0; j < kv_tiles; ++j) {
-      const uint32_t buf = tmem_base + ((j & 1u) ? kTmemS1 : kTmemS0);
-      if (!mbar_wait(&s_full[j & 1u], (j >> 1) & 1u, kWatchOther, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t sr[kKeys];
+    PrefillItem it;
+    for (uint32_t k = 0; ok && next_item(p, k, it); ++k) {
+      const uint32_t q_local = it.qt * 128 + row;  // query position in the sequence
+      float m_used = -INFINITY, l = 0.f;  // m_used: raw-score units
+      for (uint32_t j = 0; j < it.kv_tiles; ++j, ++g) {
+        const uint32_t buf = tmem_base + ((g & 1u) ? kTmemS1 : kTmemS0);
+        if (!mbar_wait(&s_full[g & 1u], (g >> 1) & 1u, kWatchOther, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t sr[kKeys];
 #pragma unroll
-      for (uint32_t c32 = 0; c32 < kKeys / 32; ++c32)
-        tmem_ld_32x32b_x32(buf + lane_addr + c32 * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c32 * 32));
-      tmem_wait_ld();
-      if (j >= first_masked) {
-        // Keys past the query, and past the sequence end, are masked.
+        for (uint32_t c32 = 0; c32 < kKeys / 32; ++c32)
+          tmem_ld_32x32b_x32(buf + lane_addr + c32 * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c32 * 32));
+        tmem_wait_ld();
+        if (j >= it.first_masked) {
+          // Keys past the query, and past the sequence end, are masked.
 #pragma unroll
-        for (uint32_t c = 0; c < kKeys; ++c) {
-          const uint32_t key = j * kKeys + c;
-          if (key > q_local || key >= p.tokens) sr[c] = __float_as_uint(-INFINITY);
-        }
-      }
-      // Eight independent partial maxima (short dependency chains), then combined.
-      float mxs[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mxs[i] = __uint_as_float(sr[i]);
-#pragma unroll
-      for (uint32_t c = 8; c < kKeys; ++c) mxs[c % 8] = fmaxf(mxs[c % 8], __uint_as_float(sr[c]));
-      const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                             fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
-      bool rescale = false;
-      float factor = 1.f;
-      if (m_used == -INFINITY) {
-        m_used = mx;
-      } else if ((mx - m_used) * kLog2e > kRescaleThreshold) {
-        factor = fast_exp2((m_used - mx) * kLog2e);
-        m_used = mx;
-        l *= factor;
-        rescale = true;
-      }
-      const float base = m_used == -INFINITY ? 0.f : m_used * kLog2e;
-      float sums[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
-#pragma unroll
-      for (int c16 = 0; c16 < int(kKeys / 32); ++c16) {
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float e0 = fast_exp2(fmaf(__uint_as_float(sr[c16 * 32 + 2 * i]), kLog2e, -base));
-          const float e1 = fast_exp2(fmaf(__uint_as_float(sr[c16 * 32 + 2 * i + 1]), kLog2e, -base));
-          sums[i % 4] += e0 + e1;
-          packed[i] = pack_bf16x2(e0, e1);
-        }
-        tmem_st_32x32b_x16(buf + lane_addr + c16 * 16, packed);
-      }
-      l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
-      // The rescale must wait for the previous P V (the only MMA writing O) to finish.
-      const bool warp_rescale = __any_sync(0xFFFFFFFFu, rescale);
-      if (warp_rescale) {
-        if (!mbar_wait(o_full, (j - 1) & 1u, kWatchOther, abort_flag)) { ok = false; }
-        if (ok) {
-          tc_fence_after();
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t orr[32];
-            tmem_ld_32x32b_x32(tmem_o + lane_addr + half * 32, orr);
-            tmem_wait_ld();
-            uint32_t lo[16], hi[16];
-#pragma unroll
-            for (int d = 0; d < 16; ++d) {
-              lo[d] = __float_as_uint(__uint_as_float(orr[d]) * factor);
-              hi[d] = __float_as_uint(__uint_as_float(orr[16 + d]) * factor);
-            }
-            tmem_st_32x32b_x16(tmem_o + lane_addr + half * 32, lo);
-            tmem_st_32x32b_x16(tmem_o + lane_addr + half * 32 + 16, hi);
+          for (uint32_t c = 0; c < kKeys; ++c) {
+            const uint32_t key = j * kKeys + c;
+            if (key > q_local || key >= p.tokens) sr[c] = __float_as_uint(-INFINITY);
           }
         }
+        // Eight independent partial maxima (short dependency chains), then combined.
+        float mxs[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mxs[i] = __uint_as_float(sr[i]);
+#pragma unroll
+        for (uint32_t c = 8; c < kKeys; ++c) mxs[c % 8] = fmaxf(mxs[c % 8], __uint_as_float(sr[c]));
+        const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                               fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+        bool rescale = false;
+        float factor = 1.f;
+        if (m_used == -INFINITY) {
+          m_used = mx;
+        } else if ((mx - m_used) * kLog2e > kRescaleThreshold) {
+          factor = fast_exp2((m_used - mx) * kLog2e);
+          m_used = mx;
+          l *= factor;
+          rescale = true;
+        }
+        const float base = m_used == -INFINITY ? 0.f : m_used * kLog2e;
+        float sums[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
+#pragma unroll
+        for (int c16 = 0; c16 < int(kKeys / 32); ++c16) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float e0 = fast_exp2(fmaf(__uint_as_float(sr[c16 * 32 + 2 * i]), kLog2e, -base));
+            const float e1 = fast_exp2(fmaf(__uint_as_float(sr[c16 * 32 + 2 * i + 1]), kLog2e, -base));
+            sums[i % 4] += e0 + e1;
+            packed[i] = pack_bf16x2(e0, e1);
+          }
+          tmem_st_32x32b_x16(buf + lane_addr + c16 * 16, packed);
+        }
+        l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
+        // The rescale must wait for the previous P V (the only MMA writing O) to finish.
+        const bool warp_rescale = __any_sync(0xFFFFFFFFu, rescale);
+        if (warp_rescale) {
+          if (!mbar_wait(o_full, (g - 1) & 1u, kWatchOther, abort_flag)) { ok = false; }
+          if (ok) {
+            tc_fence_after();
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              uint32_t orr[32];
+              tmem_ld_32x32b_x32(tmem_o + lane_addr + half * 32, orr);
+              tmem_wait_ld();
+              uint32_t lo[16], hi[16];
+#pragma unroll
+              for (int d = 0; d < 16; ++d) {
+                lo[d] = __float_as_uint(__uint_as_float(orr[d]) * factor);
+                hi[d] = __float_as_uint(__uint_as_float(orr[16 + d]) * factor);
+              }
+              tmem_st_32x32b_x16(tmem_o + lane_addr + half * 32, lo);
+              tmem_st_32x32b_x16(tmem_o + lane_addr + half * 32 + 16, hi);
+            }
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[g & 1u]);
+        if (!ok) break;
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[j & 1u]);
-      if (!ok) break;
-    }
-    // O is final once every MMA has completed. o_full cannot say so here: a softmax warp may finish the last tile
-    // while another is still on the one before, so the next-to-last P V may not even be issued yet, and a parity
-    // wait on o_full would then see the completed phase two steps back and return at once. final_bar completes
-    // exactly once, after the MMA thread has issued the last P V (which needs every warp's last P).
-    if (ok && mbar_wait(final_bar, 0, kWatchOther, abort_flag)) {
-      tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      // The item's O is final once its last P V has completed. o_full cannot say so here: a softmax warp may finish
+      // the last tile while another is still on the one before, so the next-to-last P V may not even be issued yet,
+      // and a parity wait on o_full would then see the completed phase two steps back and return at once. o_done
+      // completes once per item, after the MMA thread has issued the item's last P V (which needs every warp's P).
+      if (ok && !mbar_wait(o_done, k & 1u, kWatchOther, abort_flag)) ok = false;
+      if (ok) {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t orr[32];
-        tmem_ld_32x32b_x32(tmem_o + lane_addr + half * 32, orr);
-        tmem_wait_ld();
-        if (q_local < p.tokens) {
-          uint32_t w[16];
+        for (int half = 0; half < 2; ++half) {
+          uint32_t orr[32];
+          tmem_ld_32x32b_x32(tmem_o + lane_addr + half * 32, orr);
+          tmem_wait_ld();
+          if (q_local < p.tokens) {
+            uint32_t w[16];
 #pragma unroll
-          for (int d = 0; d < 16; ++d)
-            w[d] = pack_bf16x2(__uint_as_float(orr[2 * d]) * inv, __uint_as_float(orr[2 * d + 1]) * inv);
-          if constexpr (PACKED) {
-            // dims half*32 .. +31 are feature tiles h*4 + 2*half and +1 of the query's block
-            uint8_t* base_ptr = reinterpret_cast<uint8_t*>(p.out) + size_t(q_local >> 5) * p.block_bytes +
-                                size_t(h * 4 + 2 * half) * 1024 + (q_local & 31u) * 32;
-            uint4* t0 = reinterpret_cast<uint4*>(base_ptr);
-            uint4* t1 = reinterpret_cast<uint4*>(base_ptr + 1024);
-            t0[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            t0[1] = make_uint4(w[4], w[5], w[6], w[7]);
-            t1[0] = make_uint4(w[8], w[9], w[10], w[11]);
-            t1[1] = make_uint4(w[12], w[13], w[14], w[15]);
-          } else {
-            uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t(s) * p.tokens + q_local) * (p.heads * 64) + h * 64 +
-                                                  half * 32);
-            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-            dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
-            dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
+            for (int d = 0; d < 16; ++d)
+              w[d] = pack_bf16x2(__uint_as_float(orr[2 * d]) * inv, __uint_as_float(orr[2 * d + 1]) * inv);
+            if constexpr (PACKED) {
+              // dims half*32 .. +31 are feature tiles h*4 + 2*half and +1 of the query's block
+              uint8_t* base_ptr = reinterpret_cast<uint8_t*>(p.out) + size_t(q_local >> 5) * p.block_bytes +
+                                  size_t(it.h * 4 + 2 * half) * 1024 + (q_local & 31u) * 32;
+              uint4* t0 = reinterpret_cast<uint4*>(base_ptr);
+              uint4* t1 = reinterpret_cast<uint4*>(base_ptr + 1024);
+              t0[0] = make_uint4(w[0], w[1], w[2], w[3]);
+              t0[1] = make_uint4(w[4], w[5], w[6], w[7]);
+              t1[0] = make_uint4(w[8], w[9], w[10], w[11]);
+              t1[1] = make_uint4(w[12], w[13], w[14], w[15]);
+            } else {
+              uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t(it.s) * p.tokens + q_local) * (p.heads * 64) +
+                                                    it.h * 64 + half * 32);
+              dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+              dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+              dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
+              dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
+            }
           }
         }
       }
     }
   }
 
-  // A grid of several waves lets dependents start only as its last wave drains, so they take no SM a later CTA of
-  // this grid needs.
   if (!p.early) pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
@@ -343,6 +400,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 }  // namespace tempo
 
 using namespace tempo;
+
+// Persistent CTAs: one per item up to kCtasPerSm per SM.
+static uint32_t prefill_grid(uint64_t items) {
+  const uint64_t slots = uint64_t(sm_count()) * kCtasPerSm;
+  return uint32_t(items < slots ? items : slots);
+}
 
 extern "C" tempo_status tempo_block_attention(const void* constants, void* fused, uint32_t tokens, uint32_t heads,
                                               uint32_t head, void* stream) {
@@ -371,10 +434,10 @@ extern "C" tempo_status tempo_block_attention(const void* constants, void* fused
   p.heads = heads;
   p.q_tiles = (tokens + 127) / 128;
   p.block_bytes = block_bytes;
-  p.early = single_wave(uint64_t(p.q_tiles) * heads, kCtasPerSm);
+  p.early = 1;  // the persistent grid is resident at once
   if ((s = set_smem(reinterpret_cast<const void*>(attention_prefill_kernel<true>), kSmem))) return s;
-  return launch(attention_prefill_kernel<true>, dim3(p.q_tiles * heads), dim3(kThreads), kSmem,
-                static_cast<cudaStream_t>(stream), 1, "attention_prefill_kernel<packed>", map_q, map_kv, p);
+  return launch(attention_prefill_kernel<true>, dim3(prefill_grid(uint64_t(p.q_tiles) * heads)), dim3(kThreads),
+                kSmem, static_cast<cudaStream_t>(stream), 1, "attention_prefill_kernel<packed>", map_q, map_kv, p);
 }
 
 extern "C" tempo_status tempo_attention_prefill(const void* qkv, void* out, uint32_t seqs, uint32_t tokens,
@@ -401,10 +464,10 @@ extern "C" tempo_status tempo_attention_prefill(const void* qkv, void* out, uint
   p.tokens = tokens;
   p.heads = heads;
   p.q_tiles = (tokens + 127) / 128;
-  const uint64_t ctas = uint64_t(p.q_tiles) * heads * seqs;
-  if (ctas > 0x7FFFFFFFull) return fail(TEMPO_ERR_VALUE, "tempo_attention_prefill: too many tiles");
-  p.early = single_wave(ctas, kCtasPerSm);
+  const uint64_t items = uint64_t(p.q_tiles) * heads * seqs;
+  if (items > 0x7FFFFFFFull) return fail(TEMPO_ERR_VALUE, "tempo_attention_prefill: too many tiles");
+  p.early = 1;  // the persistent grid is resident at once
   if ((s = set_smem(reinterpret_cast<const void*>(attention_prefill_kernel<false>), kSmem))) return s;
-  return launch(attention_prefill_kernel<false>, dim3(uint32_t(ctas)), dim3(kThreads), kSmem,
+  return launch(attention_prefill_kernel<false>, dim3(prefill_grid(items)), dim3(kThreads), kSmem,
                 static_cast<cudaStream_t>(stream), 1, "attention_prefill_kernel<rowmajor>", map_q, map_kv, p);
 }
