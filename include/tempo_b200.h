@@ -261,7 +261,7 @@ tempo_status tempo_lm_head_argmax_noalloc(const void* hidden, uint32_t ld_hidden
 
 /* Calibration (no counterpart in the reference): reads `bytes` (rounded down to whole groups of 16-byte words per
  * thread) from `src` with streaming loads and writes one 16-byte word per thread into `sink`, which holds
- * tempo_stream_read_threads() words. Its rate is the HBM read ceiling the bandwidth-bound kernels are judged against. */
+ * tempo_stream_read_threads() words. Its rate is the HBM read ceiling the bandwidth-bound kernels are measured against. */
 tempo_status tempo_stream_read_threads(uint32_t* threads);
 tempo_status tempo_stream_read(const void* src, uint64_t bytes, void* sink, void* stream);
 

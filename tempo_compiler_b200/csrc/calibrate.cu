@@ -1,5 +1,5 @@
 // Calibration: the HBM read bandwidth a streaming kernel can reach on this GPU, the ceiling against which the
-// bandwidth-bound kernels (decode attention above all) are judged. Not part of the reference's surface.
+// bandwidth-bound kernels (decode attention above all) are measured. Not part of the reference's surface.
 #include <cuda_runtime.h>
 
 #include "common.cuh"
