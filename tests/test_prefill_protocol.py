@@ -1,0 +1,163 @@
+"""A model check, on the CPU, of the barrier protocol of the persistent prefill attention kernel.
+
+`tempo_compiler_b200/csrc/attention_prefill.cu` runs three roles per CTA over a sequence of (query tile, head,
+sequence) items: one thread issues the tensor-core work (S = Q K^T into two alternating TMEM buffers, then O += P V),
+four softmax warps turn each S into P in place and may rescale O, and the tensor pipe completes the issued work in
+order, each `tcgen05.commit` arriving on its mbarrier once everything issued before it has completed. The waits are
+parity waits: `mbarrier.try_wait.parity P` succeeds as soon as the barrier's current phase parity differs from P,
+so a wait is only right while the barrier is at most one phase short of the phase it means.
+
+The model below restates that protocol (issue order, the barriers, their arrival counts and the parities each role
+waits for) and runs it under many random schedules in which the warps drift apart and the tensor pipe lags. Every
+shared-state access is checked against what it needs: a warp reads S_g only once S_g has completed and before S_{g+2}
+is issued over it, P V_g is issued only once every warp has written P_g, a rescale touches O only between P V_{g-1}'s
+completion and P V_g's issue, and an item's output read sees every P V of the item completed.
+
+The kernel's final O read waits on `o_done`, committed once per item after the item's last P V. An earlier form waited
+on the per-tile O barrier with the last tile's parity; a warp that finished the last tile while another was still on
+the one before then saw the phase completed two steps back and read O early. The model finds that schedule, so the
+check is shown to bite.
+"""
+
+from __future__ import annotations
+
+import random
+
+import pytest
+
+
+class Barrier:
+    """An mbarrier: a phase completes when `count` arrivals have been made in it."""
+
+    def __init__(self, count: int) -> None:
+        self.count, self.pending, self.phase = count, 0, 0
+
+    def arrive(self) -> None:
+        self.pending += 1
+        if self.pending == self.count:
+            self.pending = 0
+            self.phase += 1
+
+    def parity_done(self, parity: int) -> bool:
+        # try_wait.parity: true once the current phase's parity differs from the one waited for.
+        return (self.phase & 1) != parity
+
+
+class Violation(AssertionError):
+    pass
+
+
+def run_schedule(items: list[int], warps: int, seed: int, final_wait: str) -> None:
+    """Runs one CTA's items (key tiles per item) under a random schedule; raises Violation on a bad access."""
+    rng = random.Random(seed)
+    s_full = [Barrier(1), Barrier(1)]
+    p_full = [Barrier(warps), Barrier(warps)]
+    o_full, o_done = Barrier(1), Barrier(1)
+    queue: list[tuple] = []        # issued tensor-pipe work, completed in order
+    issued: set[tuple] = set()     # ("S", g) / ("PV", g) issued
+    completed: set[tuple] = set()  # the same, completed
+    p_written: dict[int, set[int]] = {}
+    tile_item = [k for k, tiles in enumerate(items) for _ in range(tiles)]
+    first_tile = [sum(items[:k]) for k in range(len(items))]
+
+    def check(condition: bool, what: str) -> None:
+        if not condition:
+            raise Violation(what)
+
+    def issue(op: tuple, *commits: Barrier) -> None:
+        if op[0] == "S" and op[1] >= 2:
+            check(("PV", op[1] - 2) in issued, f"S_{op[1]} issued over P_{op[1] - 2} before its P V")
+        if op[0] == "PV":
+            check(p_written.get(op[1], set()) == set(range(warps)), f"P V_{op[1]} issued before every warp wrote P")
+        issued.add(op)
+        queue.append(op)
+        for bar in commits:
+            queue.append(("commit", bar))
+
+    def mma():
+        g = 0
+        for tiles in items:
+            issue(("S", g), s_full[g & 1])
+            for j in range(tiles):
+                if j + 1 < tiles:
+                    issue(("S", g + 1), s_full[(g + 1) & 1])
+                while not p_full[g & 1].parity_done((g >> 1) & 1):
+                    yield
+                commits = [o_full, o_done] if j + 1 == tiles else [o_full]
+                issue(("PV", g), *commits)
+                g += 1
+                yield
+
+    def softmax(w: int):
+        g = 0
+        for k, tiles in enumerate(items):
+            for j in range(tiles):
+                while not s_full[g & 1].parity_done((g >> 1) & 1):
+                    yield
+                check(("S", g) in completed, f"warp {w} read S_{g} before it completed")
+                check(("S", g + 2) not in issued, f"warp {w} read S_{g} after S_{g + 2} was issued over it")
+                yield
+                p_written.setdefault(g, set()).add(w)
+                if j >= 1 and rng.random() < 0.3:  # the row maximum grew: rescale O
+                    while not o_full.parity_done((g - 1) & 1):
+                        yield
+                    check(("PV", g - 1) in completed, f"warp {w} rescaled O before P V_{g - 1} completed")
+                    check(("PV", g) not in issued, f"warp {w} rescaled O after P V_{g} was issued")
+                    yield
+                p_full[g & 1].arrive()
+                g += 1
+                yield
+            if final_wait == "o_done":
+                while not o_done.parity_done(k & 1):
+                    yield
+            else:  # the earlier form: the per-tile O barrier with the last tile's parity
+                while not o_full.parity_done((g - 1) & 1):
+                    yield
+            for t in range(first_tile[k], g):
+                check(("PV", t) in completed, f"warp {w} read item {k}'s O before P V_{t} completed")
+            check(all(tile_item[t] == k for t in range(first_tile[k], g)), "tile bookkeeping")
+            yield
+
+    roles = {"mma": mma(), **{f"warp{w}": softmax(w) for w in range(warps)}}
+    live = dict(roles)
+    for _ in range(200000):
+        actors = list(live)
+        if queue:
+            actors += ["pipe"] * 2
+        if not actors:
+            break
+        actor = rng.choice(actors)
+        if actor == "pipe":
+            op = queue.pop(0)
+            if op[0] == "commit":
+                op[1].arrive()
+            else:
+                completed.add(op)
+            continue
+        try:
+            next(live[actor])
+        except StopIteration:
+            del live[actor]
+    check(not live and not queue, "the schedule did not finish")
+    check(all(("PV", g) in completed for g in range(sum(items))), "P V missing")
+
+
+ITEM_SETS = [[2], [3], [4, 2], [2, 2, 2], [5, 1, 3], [1, 1, 1, 1]]
+
+
+@pytest.mark.parametrize("items", ITEM_SETS)
+def test_final_read_waits_for_every_p_v(items: list[int]) -> None:
+    for seed in range(300):
+        run_schedule(items, warps=4, seed=seed, final_wait="o_done")
+
+
+def test_the_per_tile_barrier_final_wait_is_caught() -> None:
+    """The earlier final wait reads O early under some schedule; the model finds it."""
+    found = []
+    for seed in range(2000):
+        try:
+            run_schedule([3, 2], warps=4, seed=seed, final_wait="o_full")
+        except Violation as error:
+            found.append(str(error))
+            break
+    assert found and "O before P V" in found[0], found
