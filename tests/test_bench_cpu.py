@@ -1,4 +1,4 @@
-"""bench.py's host-side pieces that need no GPU: the clock-sample window and the job's GPU indices."""
+"""bench.py's host-side pieces that need no GPU: the clock-sample window, the job's GPU indices and the reference arm."""
 
 from __future__ import annotations
 
@@ -45,3 +45,42 @@ def test_job_gpus_follow_the_visible_devices(monkeypatch) -> None:
     assert bench._job_gpu_indices(4) == [0, 1, 2, 3]
     monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "4,5,6,7")
     assert bench._job_gpu_indices(2) == [4, 5]
+
+
+def _reference_arm(extra_env: dict | None = None):
+    import json
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ, **(extra_env or {}))
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    done = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--impl", "reference", "--steps", "1",
+                           "--warmup", "1", "--cpu-prompt", "16", "--cpu-decode", "1"],
+                          capture_output=True, text=True, timeout=600, env=env, cwd=root)
+    assert done.returncode == 0, done.stderr[-2000:]
+    lines = [line for line in done.stdout.splitlines() if line.startswith("{")]
+    return [json.loads(line) for line in lines]
+
+
+def test_reference_arm_prints_one_contract_line() -> None:
+    """The reference arm (the reference's host path, timed on the host cores) needs no GPU: one JSON line with the
+    workload's metric, its own CPU-baseline record and an end-to-end record with no host-device traffic."""
+    import json
+    import os
+    lines = _reference_arm({"RANK": "0"})
+    assert len(lines) == 1
+    line = lines[0]
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    with open(os.path.join(root, "BASELINE.json")) as f:
+        metric = json.load(f)["metric"]
+    assert line["impl"] == "reference" and line["metric"] == metric and line["unit"] == "tok/s"
+    assert line["higher_is_better"] is True and line["steps"] == 1 and line["value"] > 0
+    baseline = line["cpu_baseline"]
+    assert baseline["kind"] == "port" and baseline["cores"] >= 1 and baseline["value"] == line["value"]
+    assert "16-token prefill" in baseline["sample"]
+    assert line["e2e"] == {"value": line["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_runs_on_rank_zero_only() -> None:
+    assert _reference_arm({"RANK": "1", "WORLD_SIZE": "2"}) == []
