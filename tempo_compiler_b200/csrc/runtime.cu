@@ -17,6 +17,7 @@
 #include <string>
 #include <thread>
 #include <unordered_map>
+#include <utility>
 
 #include "host.hpp"
 
@@ -98,14 +99,18 @@ int sm_count() {
   return count;
 }
 
+// A function attribute belongs to the device's context, so it is set once per (device, kernel).
 tempo_status set_smem(const void* kernel, int bytes) {
   static std::mutex mu;
-  static std::set<const void*> done;
+  static std::set<std::pair<int, const void*>> done;
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
   std::lock_guard<std::mutex> lock(mu);
-  if (done.count(kernel)) return TEMPO_OK;
-  const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (done.count({device, kernel})) return TEMPO_OK;
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute(max dynamic shared memory)");
-  done.insert(kernel);
+  done.insert({device, kernel});
   return TEMPO_OK;
 }
 
