@@ -25,44 +25,19 @@ import random
 
 import pytest
 
-
-class Barrier:
-    """An mbarrier: a phase completes when `count` arrivals have been made in it."""
-
-    def __init__(self, count: int) -> None:
-        self.count, self.pending, self.phase = count, 0, 0
-
-    def arrive(self) -> None:
-        self.pending += 1
-        if self.pending == self.count:
-            self.pending = 0
-            self.phase += 1
-
-    def parity_done(self, parity: int) -> bool:
-        # try_wait.parity: true once the current phase's parity differs from the one waited for.
-        return (self.phase & 1) != parity
-
-
-class Violation(AssertionError):
-    pass
+from _protocol import Barrier, Pipe, Violation, check, run, wait
 
 
 def run_schedule(items: list[int], warps: int, seed: int, final_wait: str) -> None:
     """Runs one CTA's items (key tiles per item) under a random schedule; raises Violation on a bad access."""
     rng = random.Random(seed)
-    s_full = [Barrier(1), Barrier(1)]
-    p_full = [Barrier(warps), Barrier(warps)]
-    o_full, o_done = Barrier(1), Barrier(1)
-    queue: list[tuple] = []        # issued tensor-pipe work, completed in order
-    issued: set[tuple] = set()     # ("S", g) / ("PV", g) issued
-    completed: set[tuple] = set()  # the same, completed
+    tensor = Pipe()
+    s_full = [Barrier(1, "s_full0"), Barrier(1, "s_full1")]
+    p_full = [Barrier(warps, "p_full0"), Barrier(warps, "p_full1")]
+    o_full, o_done = Barrier(1, "o_full"), Barrier(1, "o_done")
+    issued: set[tuple] = set()  # ("S", g) / ("PV", g) issued
     p_written: dict[int, set[int]] = {}
-    tile_item = [k for k, tiles in enumerate(items) for _ in range(tiles)]
     first_tile = [sum(items[:k]) for k in range(len(items))]
-
-    def check(condition: bool, what: str) -> None:
-        if not condition:
-            raise Violation(what)
 
     def issue(op: tuple, *commits: Barrier) -> None:
         if op[0] == "S" and op[1] >= 2:
@@ -70,9 +45,7 @@ def run_schedule(items: list[int], warps: int, seed: int, final_wait: str) -> No
         if op[0] == "PV":
             check(p_written.get(op[1], set()) == set(range(warps)), f"P V_{op[1]} issued before every warp wrote P")
         issued.add(op)
-        queue.append(op)
-        for bar in commits:
-            queue.append(("commit", bar))
+        tensor.push(("op", op), *(("commit", bar) for bar in commits))
 
     def mma():
         g = 0
@@ -81,8 +54,7 @@ def run_schedule(items: list[int], warps: int, seed: int, final_wait: str) -> No
             for j in range(tiles):
                 if j + 1 < tiles:
                     issue(("S", g + 1), s_full[(g + 1) & 1])
-                while not p_full[g & 1].parity_done((g >> 1) & 1):
-                    yield
+                yield from wait(lambda g=g: p_full[g & 1].parity_done((g >> 1) & 1))
                 commits = [o_full, o_done] if j + 1 == tiles else [o_full]
                 issue(("PV", g), *commits)
                 g += 1
@@ -92,54 +64,29 @@ def run_schedule(items: list[int], warps: int, seed: int, final_wait: str) -> No
         g = 0
         for k, tiles in enumerate(items):
             for j in range(tiles):
-                while not s_full[g & 1].parity_done((g >> 1) & 1):
-                    yield
-                check(("S", g) in completed, f"warp {w} read S_{g} before it completed")
+                yield from wait(lambda g=g: s_full[g & 1].parity_done((g >> 1) & 1))
+                check(("S", g) in tensor.done, f"warp {w} read S_{g} before it completed")
                 check(("S", g + 2) not in issued, f"warp {w} read S_{g} after S_{g + 2} was issued over it")
                 yield
                 p_written.setdefault(g, set()).add(w)
                 if j >= 1 and rng.random() < 0.3:  # the row maximum grew: rescale O
-                    while not o_full.parity_done((g - 1) & 1):
-                        yield
-                    check(("PV", g - 1) in completed, f"warp {w} rescaled O before P V_{g - 1} completed")
+                    yield from wait(lambda g=g: o_full.parity_done((g - 1) & 1))
+                    check(("PV", g - 1) in tensor.done, f"warp {w} rescaled O before P V_{g - 1} completed")
                     check(("PV", g) not in issued, f"warp {w} rescaled O after P V_{g} was issued")
                     yield
                 p_full[g & 1].arrive()
                 g += 1
                 yield
             if final_wait == "o_done":
-                while not o_done.parity_done(k & 1):
-                    yield
+                yield from wait(lambda k=k: o_done.parity_done(k & 1))
             else:  # the earlier form: the per-tile O barrier with the last tile's parity
-                while not o_full.parity_done((g - 1) & 1):
-                    yield
+                yield from wait(lambda g=g: o_full.parity_done((g - 1) & 1))
             for t in range(first_tile[k], g):
-                check(("PV", t) in completed, f"warp {w} read item {k}'s O before P V_{t} completed")
-            check(all(tile_item[t] == k for t in range(first_tile[k], g)), "tile bookkeeping")
+                check(("PV", t) in tensor.done, f"warp {w} read item {k}'s O before P V_{t} completed")
             yield
 
-    roles = {"mma": mma(), **{f"warp{w}": softmax(w) for w in range(warps)}}
-    live = dict(roles)
-    for _ in range(200000):
-        actors = list(live)
-        if queue:
-            actors += ["pipe"] * 2
-        if not actors:
-            break
-        actor = rng.choice(actors)
-        if actor == "pipe":
-            op = queue.pop(0)
-            if op[0] == "commit":
-                op[1].arrive()
-            else:
-                completed.add(op)
-            continue
-        try:
-            next(live[actor])
-        except StopIteration:
-            del live[actor]
-    check(not live and not queue, "the schedule did not finish")
-    check(all(("PV", g) in completed for g in range(sum(items))), "P V missing")
+    run({"mma": mma(), **{f"warp{w}": softmax(w) for w in range(warps)}}, [tensor], rng)
+    check(all(("PV", g) in tensor.done for g in range(sum(items))), "P V missing")
 
 
 ITEM_SETS = [[2], [3], [4, 2], [2, 2, 2], [5, 1, 3], [1, 1, 1, 1]]
