@@ -33,7 +33,7 @@ tempo_status encode_tmap(CUtensorMap* map, CUtensorMapDataType type, uint32_t ra
 // The number of SMs of the current device (cached).
 int sm_count();
 
-// Opts a kernel into more than 48 KB of dynamic shared memory, once per process.
+// Opts a kernel into more than 48 KB of dynamic shared memory, once per device.
 tempo_status set_smem(const void* kernel, int bytes);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
