@@ -26,6 +26,31 @@ def test_library_exports_every_declared_symbol() -> None:
         assert getattr(library, name) is not None
 
 
+def test_binding_argument_types_follow_the_header() -> None:
+    """Every declaration's parameters, in order, against the ctypes signature the binding passes: a pointer for a
+    pointer and the same width and signedness for a scalar, so no argument is truncated or misread across the C ABI."""
+    import ctypes
+
+    from tempo_compiler_b200 import lib
+    header = (ROOT / "include" / "tempo_b200.h").read_text()
+    header = re.sub(r"/\*.*?\*/", "", header, flags=re.S)
+    scalars = {"uint32_t": ctypes.c_uint32, "uint64_t": ctypes.c_uint64, "int32_t": ctypes.c_int32,
+               "int64_t": ctypes.c_int64, "int": ctypes.c_int, "float": ctypes.c_float, "double": ctypes.c_double}
+    declarations = re.findall(r"tempo_status\s+(tempo_\w+)\s*\(([^)]*)\)\s*;", header)
+    assert {name for name, _ in declarations} == set(lib.EXPORTED)
+    for name, params in declarations:
+        params = " ".join(params.split())
+        declared = [] if params in ("", "void") else [p.strip() for p in params.split(",")]
+        bound = lib._SIGNATURES[name]
+        assert len(declared) == len(bound), (name, declared, bound)
+        for param, ctype in zip(declared, bound):
+            if "*" in param:
+                assert ctype in (ctypes.c_void_p, ctypes.c_char_p) or issubclass(ctype, ctypes._Pointer), (name, param)
+            else:
+                base = param.replace("const ", "").split()[0]
+                assert scalars[base] is ctype, (name, param, ctype)
+
+
 def test_status_codes_map_to_the_reference_exceptions() -> None:
     from tempo_compiler_b200 import lib
     for status, exc in ((lib.ERR_VALUE, ValueError), (lib.ERR_MEMORY, MemoryError), (lib.ERR_KEY, KeyError),
