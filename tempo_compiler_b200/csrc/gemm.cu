@@ -1199,7 +1199,6 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   } else {
     // Epilogue: this CTA's 128 rows of each 256 x 256 tile, sixteen warps as in the row-major kernel.
     const uint32_t lane_base = 32u * (warp & 3u);
-    const uint32_t row_in_tile = lane_base + lane;
     const uint32_t group = (warp - 2) >> 2;
     constexpr uint32_t kGroupCols = kPairBN / kRowEpiGroups;
     constexpr uint32_t kCW = 32;
