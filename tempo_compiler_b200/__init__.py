@@ -9,10 +9,9 @@ Modules:
     lib       -- loads the C-ABI library (ctypes) and maps its status codes to the reference's exceptions.
     runtime   -- drop-in replacement of the reference board runtime (``minitpu*`` API) over the library.
     images    -- the image set: manifest entries with the reference's kinds and fields, and their descriptors.
-    gpt2      -- the reference's per-block layer drivers over ``runtime`` (the drop-in host path).
+    dropin    -- GPT-2 driven through ``runtime`` with one image launch per 32-token block (the drop-in host path).
     engine    -- the B200-native GPT-2 engine: resident weights, batched prefill/decode, CUDA graphs.
     weights   -- seeded random GPT-2 weights in the reference's naming scheme.
-    packing   -- the packed block layouts of the drop-in contract.
 """
 
-__all__ = ["lib", "runtime", "images", "gpt2", "engine", "weights", "packing"]
+__all__ = ["lib", "runtime", "images", "dropin", "engine", "weights"]

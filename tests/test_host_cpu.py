@@ -5,6 +5,7 @@ refused before any device work, with the reference's exception classes."""
 from __future__ import annotations
 
 import json
+import os
 import pathlib
 import re
 import struct
@@ -134,31 +135,39 @@ def test_image_set_keeps_the_reference_manifest_fields(tmp_path) -> None:
             np.testing.assert_array_equal(constants, ob.causal_constants_words())
 
 
-def test_dropin_packers_agree_with_the_oracle() -> None:
-    from tempo_compiler_b200 import gpt2
+def test_dropin_layouts_agree_with_the_oracle() -> None:
+    """The drop-in driver's host layouts equal the oracle's restatement of the reference's packers."""
+    from tempo_compiler_b200 import dropin
     rng = np.random.default_rng(9)
     act = rng.standard_normal((32, 40)).astype(np.float32)
     wts = rng.standard_normal((40, 24)).astype(np.float32)
-    bias = rng.standard_normal(24).astype(np.float32)
-    np.testing.assert_array_equal(gpt2.pack_activations(act), ob.pack_activations(act))
-    np.testing.assert_array_equal(gpt2.pack_weights(wts), ob.pack_weights(wts))
-    np.testing.assert_array_equal(gpt2.pack_bias(bias), ob.pack_bias(bias))
-    masks = gpt2.decode_mask_tiles(keys=64, length=49)
-    np.testing.assert_array_equal(masks, ob.decode_mask_tiles(keys=64, length=49))
-    np.testing.assert_array_equal(gpt2.pack_attention_constants(initial_maximum=-1e30, constants=(1.5,), masks=masks),
-                                  ob.pack_attention_constants(initial_maximum=-1e30, constants=(1.5,), masks=masks))
+    bias = rng.standard_normal(32).astype(np.float32)
+    np.testing.assert_array_equal(dropin.tile_major(act), ob.pack_activations(act))
+    np.testing.assert_array_equal(dropin.tile_major(wts), ob.pack_weights(wts))
+    np.testing.assert_array_equal(dropin.bias_rows(bias), ob.pack_bias(bias))
+    np.testing.assert_array_equal(dropin.to_words(act), ob.bf16_bits(act))
+    for keys, length, stated, transposed in ((64, 49, (), True), (256, 200, (1.5,), True), (64, 1, (), False)):
+        masks = ob.decode_mask_tiles(keys=keys, length=length)
+        if transposed:
+            masks = np.ascontiguousarray(masks.swapaxes(-1, -2))
+        expected = ob.pack_attention_constants(initial_maximum=-1e30, constants=stated, masks=masks).reshape(-1)
+        got = dropin.mask_tiles(keys=keys, length=length, entering=-1e30, stated=stated, transposed=transposed)
+        np.testing.assert_array_equal(got, expected)
+    words = dropin.tile_major(act)
+    np.testing.assert_array_equal(dropin.from_tile_major(words, 32, 48)[:, :40], ob.bf16_grid(act))
 
 
 def test_reference_drivers_import_against_the_runtime_shim() -> None:
     """The maintainer's binding: the reference's own drivers import with this runtime installed as ``runtime``.
 
-    Only the import surface is checked here (no launch); it needs the reference tree, so it is skipped where that is
-    absent."""
+    Only the import surface is checked here (no launch); it needs the reference's checkout, named by the environment
+    variable TEMPO_REFERENCE_DIR, and is skipped without it."""
     import importlib
     import sys
-    reference = pathlib.Path("/root/reference/board_package")
-    if not reference.exists():
-        pytest.skip("the reference tree is not present")
+    root = os.environ.get("TEMPO_REFERENCE_DIR")
+    if not root or not (pathlib.Path(root) / "board_package").is_dir():
+        pytest.skip("TEMPO_REFERENCE_DIR does not name the reference project's checkout")
+    reference = pathlib.Path(root) / "board_package"
     from tempo_compiler_b200 import runtime
     saved = {name: sys.modules.get(name) for name in ("runtime", "gpt2_inference", "bf16", "tokenizer")}
     sys.modules["runtime"] = runtime
