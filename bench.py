@@ -42,8 +42,11 @@ def parse() -> argparse.Namespace:
     p.add_argument("--prompt", type=int, default=1024)
     p.add_argument("--decode", type=int, default=128)
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--cpu-prompt", type=int, default=512, help="prompt of the bounded CPU sample")
-    p.add_argument("--cpu-decode", type=int, default=8, help="decode steps of the bounded CPU sample")
+    p.add_argument("--cpu-prompt", type=int, default=None,
+                   help="prompt of the bounded CPU sample (default: the workload's prompt)")
+    p.add_argument("--cpu-decode", type=int, default=8, help="decode steps timed per CPU sample")
+    p.add_argument("--cpu-literal-steps", type=int, default=1,
+                   help="decode steps also timed the reference's literal way (the whole sequence recomputed)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-graph", action="store_true", help="eager decode instead of the captured CUDA graph")
     p.add_argument("--fold-layernorms", choices=["auto", "on", "off"], default="auto",
@@ -69,7 +72,10 @@ def workload(args) -> dict:
                          f"{args.decode} greedy decode steps)"),
             "sequences": args.sequences, "prompt_tokens": args.prompt, "decode_steps": args.decode,
             "parallelism": f"sequences sharded over {args.gpus} GPU(s), no collective on the data path",
-            "l2": "inputs larger than L2 (170 MB weights + the KV cache, 21.7 GB at 512 sequences)"}
+            "l2": "inputs larger than L2 (170 MB weights + the KV cache, 21.7 GB at 512 sequences)",
+            "positions": max(1024, args.prompt + args.decode),
+            "positions_note": ("GPT-2 small learns 1024 positions; sequences of prompt + decode tokens past that use "
+                               "a longer learned table, drawn like the other weights")}
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -85,19 +91,6 @@ def blas_threads() -> int:
         return 1
 
 
-def cpu_sample(args, layers, shared) -> tuple[float, int]:
-    """Runs one bounded sample of the workload on the host: one sequence, a `cpu_prompt`-token prefill and
-    `cpu_decode` greedy steps through the reference's device-rounding host references (KV-cached chain built from
-    them). Returns (seconds, tokens processed)."""
-    from oracle.model import CachedChain
-    from tempo_compiler_b200.weights import random_token_ids
-    ids = [int(t) for t in random_token_ids(args.seed + 1000, args.cpu_prompt)]
-    chain = CachedChain(layers, shared, mode="device")
-    started = time.perf_counter()
-    chain.generate(ids, new_tokens=args.cpu_decode + 1)
-    return time.perf_counter() - started, args.cpu_prompt + args.cpu_decode
-
-
 def all_host_threads() -> None:
     """Lets the BLAS pool use every core this process may run on (torchrun starts each rank with
     OMP_NUM_THREADS=1; the reference arm runs on rank 0 alone)."""
@@ -108,29 +101,112 @@ def all_host_threads() -> None:
         pass
 
 
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def model(args):
+    """The workload's random-init GPT-2 small. Its sequences reach prompt + decode positions; past GPT-2's 1024
+    learned positions the table grows, drawn like the rest (its first 1024 rows are the 1024-row table's)."""
+    from tempo_compiler_b200.weights import GPT2Shape, random_gpt2
+    return random_gpt2(args.seed, GPT2Shape(positions=max(1024, args.prompt + args.decode)))
+
+
+class CpuSample:
+    """The reference's host path on one sequence of the workload's shape, on this machine's cores.
+
+    The reference's host references (board_package/references.py, restated by the oracle in device mode: BF16
+    accumulation, table GELU) run the prompt once; decode steps then run through the KV-cached restatement of the
+    same references (oracle.model.CachedChain), each sample from a copy of the post-prefill state, so every sample
+    decodes the positions right after the prompt. A sequence's time is extrapolated: the prefill plus `decode`
+    times the mean step. The reference's own decode check recomputes the whole sequence for each token
+    (board_package/board_checks.py:467-474); `literal_steps` such steps are timed beside it."""
+
+    def __init__(self, args, layers, shared) -> None:
+        import copy
+        from oracle.model import CachedChain, forward_logits
+        from tempo_compiler_b200.weights import random_token_ids
+        self.args = args
+        self.prompt = args.prompt if args.cpu_prompt is None else args.cpu_prompt
+        self.ids = [int(t) for t in random_token_ids(args.seed + 1000, self.prompt)]
+        chain = CachedChain(layers, shared, mode="device")
+        started = time.perf_counter()
+        logits = chain.prefill(self.ids)
+        self.prefill_s = time.perf_counter() - started
+        self.first = int(np.argmax(logits))
+        self.state = chain
+        self._copy = copy.deepcopy
+        self.step_seconds: list[float] = []
+        self.literal_s = None
+        if args.cpu_literal_steps > 0:
+            started = time.perf_counter()
+            for k in range(args.cpu_literal_steps):
+                forward_logits(self.ids + [self.first] * (k + 1), layers, shared, mode="device")
+            self.literal_s = (time.perf_counter() - started) / args.cpu_literal_steps
+
+    def decode_sample(self) -> float:
+        """Times `cpu_decode` greedy steps after the prompt; returns their seconds."""
+        chain = self._copy(self.state)
+        token = self.first
+        started = time.perf_counter()
+        for _ in range(self.args.cpu_decode):
+            token = int(np.argmax(chain.step(token)))
+        seconds = time.perf_counter() - started
+        self.step_seconds.append(seconds / max(1, self.args.cpu_decode))
+        return seconds
+
+    def per_sequence_s(self) -> float:
+        mean_step = sum(self.step_seconds) / len(self.step_seconds) if self.step_seconds else 0.0
+        return self.prefill_s + self.args.decode * mean_step
+
+    def value(self) -> float:
+        return (self.prompt + self.args.decode) / self.per_sequence_s()
+
+    def record(self) -> dict:
+        mean_step = sum(self.step_seconds) / len(self.step_seconds) if self.step_seconds else 0.0
+        threads = blas_threads()
+        out = {"value": self.value(), "unit": "tok/s", "cores": threads, "kind": "port",
+               "host_cpus": os.cpu_count(), "cpu_model": cpu_model(), "blas_threads": threads,
+               "prefill_s": self.prefill_s, "decode_step_s": mean_step,
+               "sample": (f"KV-cached restatement (extrapolated per sequence): 1 sequence of the workload's shape, a "
+                          f"{self.prompt}-token prefill timed once ({self.prefill_s:.1f} s) plus {self.args.decode} "
+                          f"decode steps extrapolated from {len(self.step_seconds)} x {self.args.cpu_decode} timed "
+                          f"steps (mean {mean_step * 1000:.0f} ms, positions {self.prompt}-"
+                          f"{self.prompt + self.args.cpu_decode - 1}); the reference's host references "
+                          f"(board_package/references.py semantics: BF16 accumulation, table GELU) restated in numpy")}
+        if self.literal_s is not None:
+            out["literal_full_recompute_s_per_token"] = self.literal_s
+            out["literal_full_recompute_tok_s"] = 1.0 / self.literal_s
+            out["sample"] += (f"; the reference's literal decode (whole sequence recomputed per token, "
+                              f"board_checks.py:467-474) measured at {self.literal_s:.1f} s per token at "
+                              f"{self.prompt + 1} tokens")
+        return out
+
+
 def reference_arm(args) -> int:
     if int(os.environ.get("RANK", "0")) != 0:
         return 0
     all_host_threads()
-    from tempo_compiler_b200.weights import random_gpt2
-    layers, shared = random_gpt2(args.seed)
+    layers, shared = model(args)
+    sample = CpuSample(args, layers, shared)
     for _ in range(args.warmup):
-        cpu_sample(args, layers, shared)
-    seconds, tokens = 0.0, 0
-    for _ in range(args.steps):
-        s, t = cpu_sample(args, layers, shared)
-        seconds += s
-        tokens += t
-    value = tokens / seconds
-    sample = (f"1 sequence: {args.cpu_prompt}-token prefill + {args.cpu_decode} greedy decode steps per step, "
-              f"numpy float64/BF16-rounding host references (board_package/references.py semantics)")
+        sample.decode_sample()
+    sample.step_seconds.clear()
+    seconds = sum(sample.decode_sample() for _ in range(args.steps))
+    record = sample.record()
+    value = record["value"]
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * seconds / args.steps, "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * seconds / max(1, args.steps), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16 storage, float64/BF16-rounded arithmetic",
             "data": "synthetic (seeded uniform token ids, random-init weights ~N(0,0.02))", "config": workload(args),
-            "impl": "reference",
-            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
-                             "sample": sample},
+            "impl": "reference", "cpu_baseline": record,
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -262,13 +338,13 @@ def b200_arm(args) -> int:
     from tempo_compiler_b200.engine import Engine
     from tempo_compiler_b200.sharding import gather_tokens, shard
     from tempo_compiler_b200.sharding import max_over_ranks as _max_over_ranks
-    from tempo_compiler_b200.weights import random_gpt2, random_token_ids
+    from tempo_compiler_b200.weights import random_token_ids
 
     def max_over_ranks(value: float) -> float:
         return _max_over_ranks(value, device)
 
     lib.load()
-    layers, shared = random_gpt2(args.seed)
+    layers, shared = model(args)
     first, per_rank = shard(args.sequences, world, rank)
     if per_rank == 0:
         raise SystemExit(f"{args.sequences} sequences leave rank {rank} of {world} without work")
@@ -307,6 +383,7 @@ def b200_arm(args) -> int:
     torch.cuda.synchronize()
     if clocks is not None:
         clocks.mark_end()
+    timed_tokens = engine.tokens.cpu().numpy().copy()
     barrier()
     clock_info = clocks.stop() if clocks is not None else None
     ms = max_over_ranks(start.elapsed_time(end))
@@ -318,8 +395,11 @@ def b200_arm(args) -> int:
     barrier()
     torch.cuda.synchronize()
     e2e_start.record(stream)
+    first_tokens = None
     for _ in range(args.steps):
         tokens = engine.generate(ids, args.decode, graph=graph)
+        if first_tokens is None:
+            first_tokens = tokens.copy()
     e2e_end.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -335,7 +415,10 @@ def b200_arm(args) -> int:
     roof = _decode_attention_roofline(engine, stream, measured, source)
     gemm_roof = _gemm_roofline(engine, stream, measured, source)
     watchdog = int(max_over_ranks(float(ops.watchdog())))
-    all_tokens = gather_tokens(torch.from_numpy(np.ascontiguousarray(tokens)), args.sequences, device)
+    # the same job repeated gives the same tokens: the device-timed run, the first and the last end-to-end run
+    runs = [gather_tokens(torch.from_numpy(np.ascontiguousarray(t)), args.sequences, device)
+            for t in (timed_tokens, first_tokens, tokens)]
+    all_tokens = runs[-1]
 
     line = None
     if rank == 0:
@@ -351,13 +434,13 @@ def b200_arm(args) -> int:
                 "clocks": clock_info, "roofline": roof, "gemm_roofline": gemm_roof,
                 "phases_ms_rank0": {"prefill": prefill_ms, "decode": decode_ms},
                 "decode_graph": graph, "watchdog": watchdog,
-                "tokens_checksum": int(all_tokens.to(torch.int64).sum().item())}
+                "tokens_checksum": int(all_tokens.to(torch.int64).sum().item()),
+                "tokens_checksums_of_repeats": [int(r.to(torch.int64).sum().item()) for r in runs],
+                "tokens_repeat_identical": all(bool(torch.equal(r, runs[0])) for r in runs)}
         if world == 1 and not args.no_cpu_baseline:
-            seconds, count = cpu_sample(args, layers, shared)
-            line["cpu_baseline"] = {
-                "value": count / seconds, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
-                "sample": (f"1 sequence: {args.cpu_prompt}-token prefill + {args.cpu_decode} greedy decode steps, "
-                           f"numpy host references (board_package/references.py semantics), {seconds:.1f} s")}
+            sample = CpuSample(args, layers, shared)
+            sample.decode_sample()
+            line["cpu_baseline"] = sample.record()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

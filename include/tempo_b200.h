@@ -120,6 +120,12 @@ tempo_status tempo_stats(uint64_t* launches, uint64_t* arena_used);
 /* Reads and clears the device watchdog: non-zero names the bounded wait that expired in a kernel. */
 tempo_status tempo_watchdog(int32_t* code);
 
+/* Failure-detection probe, the device half of the reference's drain and timeout tests
+ * (board_package/tests/test_drain.py:23-159, runtime/memcpy.py:289-312): one CTA waits on an mbarrier that
+ * completes only when `arrive` is non-zero, giving up after `limit_ns` (at most 10 s) as every pipeline wait does,
+ * with watchdog code 6. `stream` NULL means the runtime's stream, the one tempo_sync waits for. */
+tempo_status tempo_wait_probe(uint32_t arrive, uint64_t limit_ns, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------------------
  * 2. Per-32-token-block tile ops on the packed layouts, with 64-bit device pointers. One call is one launch of the
  *    corresponding image (board_package/gpt2_inference.py:474-640,981-1039,1204-1209).

@@ -28,6 +28,7 @@ from oracle.references import (
     gelu_device,
     layernorm_device,
     layernorm_f64,
+    widened,
 )
 
 END_OF_TEXT: int = 50256
@@ -53,7 +54,7 @@ def lm_head(normalised, shared: dict, mode: str) -> NDArray:
     in device mode as the reference does, float64 in exact mode."""
     if mode == "device":
         return np.asarray(normalised, dtype=np.float32) @ shared["wte"].T
-    return np.asarray(normalised, dtype=np.float64) @ shared["wte"].T.astype(np.float64)
+    return widened(shared["wte"]) @ np.asarray(normalised, dtype=np.float64)
 
 
 def block(rows, weights: dict, mode: str) -> NDArray[np.float32]:

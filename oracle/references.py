@@ -33,15 +33,32 @@ from oracle.bf16 import (
 # ----------------------------------------------------------------------------------------------------------------
 
 
+_WIDE: dict[int, tuple[NDArray, NDArray[np.float64]]] = {}
+
+
+def widened(matrix) -> NDArray[np.float64]:
+    """A weight matrix in float64, widened once and kept while the same array object is alive in the cache (the
+    oracle's chains multiply by the same weights at every decode step)."""
+    if not isinstance(matrix, np.ndarray) or matrix.size < (1 << 20):
+        return np.asarray(matrix, dtype=np.float64)
+    cached = _WIDE.get(id(matrix))
+    if cached is None or cached[0] is not matrix:
+        if len(_WIDE) >= 64:
+            _WIDE.clear()
+        cached = (matrix, matrix.astype(np.float64))
+        _WIDE[id(matrix)] = cached
+    return cached[1]
+
+
 def device_product(left, right) -> NDArray[np.float32]:
     """A product summed as the NPU sums it: each 32-deep partial exact then rounded to BF16, added into a BF16
     running sum (``_device_product``, board_package/references.py:119-140)."""
-    left = np.asarray(left, dtype=np.float32)
-    right = np.asarray(right, dtype=np.float32)
-    running = np.zeros((left.shape[0], right.shape[1]), dtype=np.float32)
+    left = np.asarray(left, dtype=np.float32).astype(np.float64)
+    wide = widened(right) if isinstance(right, np.ndarray) else np.asarray(right, dtype=np.float32).astype(np.float64)
+    running = np.zeros((left.shape[0], wide.shape[1]), dtype=np.float32)
     for start in range(0, left.shape[1], BLOCK_DEPTH):
         stop = start + BLOCK_DEPTH
-        partial = (left[:, start:stop].astype(np.float64) @ right[start:stop].astype(np.float64)).astype(np.float32)
+        partial = (left[:, start:stop] @ wide[start:stop]).astype(np.float32)
         running = bf16_grid(running + bf16_grid(partial))
     return running
 
@@ -170,7 +187,7 @@ def gemm_f64(left, right, *, bias=None, activate: bool = False) -> NDArray[np.fl
     """[GELU](left) @ right (+ bias) in float64, GELU exact-erf on BF16 inputs rounded back to BF16 as the staging
     leaves them (board_package/board_checks.py:238; tests/test_mlir_gemm.py:96-101; tests/test_mlir_padding.py:159-162)."""
     staged = gelu_exact_bf16(left) if activate else np.asarray(left, dtype=np.float32)
-    product = staged.astype(np.float64) @ np.asarray(right, dtype=np.float64)
+    product = staged.astype(np.float64) @ widened(right)
     if bias is not None:
         product = product + np.asarray(bias, dtype=np.float64)
     return product

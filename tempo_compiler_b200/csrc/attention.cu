@@ -121,8 +121,11 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* _
                                                                int32_t length_offset, uint16_t* __restrict__ out,
                                                                uint32_t heads, uint32_t capacity, uint32_t early) {
   if (early) pdl_launch_dependents();
-  pdl_wait();
   const uint32_t chunks = gridDim.x, h = blockIdx.y, s = blockIdx.z;
+  // A CTA's shared memory may be addressed by the others of its cluster only once every CTA of the cluster has
+  // started: each announces itself here and waits for the rest just before its first remote store.
+  if (chunks > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  pdl_wait();
   const uint32_t chunk = chunks > 1 ? decode_cluster_rank() : 0u;
   const uint32_t warp = warp_id(), lane = lane_id();
   const uint32_t g = lane >> 3, li = lane & 7u;
@@ -192,6 +195,7 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* _
     if (d < 64) out[size_t(s) * width + h * 64 + d] = float_to_bf16(l > 0.f ? a / l : 0.f);
     return;
   }
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   if (d < 64) {
     uint32_t remote;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(&part[chunk][0])), "r"(0u));

@@ -37,6 +37,7 @@ enum WatchdogCode : int {
   kWatchAccFull = 3,   // epilogue waiting for the accumulator
   kWatchAccEmpty = 4,  // MMA waiting for the epilogue to drain the accumulator
   kWatchOther = 5,
+  kWatchProbe = 6,     // the failure-detection probe's wait, which nothing completes unless asked to
 };
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -179,8 +180,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 }
 
 // Waits for the phase with the given parity to complete. Returns false (and records `code`) if it has not after
-// kWaitLimitNs, or if `abort` (a shared flag another role sets when it gives up) becomes non-zero.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code, volatile int* abort) {
+// `limit_ns` of global time, or if `abort` (a shared flag another role sets when it gives up) becomes non-zero.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int code, volatile int* abort,
+                                              unsigned long long limit_ns) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long start = global_ns();
@@ -188,13 +190,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
     if (mbar_try_wait(addr, parity)) return true;
     if ((spin & 255u) == 0u) {
       if (abort != nullptr && *abort) return false;
-      if (global_ns() - start > kWaitLimitNs) {
+      if (global_ns() - start > limit_ns) {
         atomicExch(&g_tempo_watchdog, code);
         if (abort != nullptr) *abort = 1;
         return false;
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code, volatile int* abort) {
+  return mbar_wait_for(bar, parity, code, abort, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------------------------------------------------------

@@ -774,6 +774,13 @@ __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// The split halves of a cluster barrier: every thread of the cluster arrives once (relaxed: it orders nothing) and
+// later waits for all the others to have arrived.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
 template <int BN, int SPLITS, int STAGES>
 __global__ void __launch_bounds__(kSplitThreads, 1)
     gemm_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -820,6 +827,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_launch_dependents();
+  // Another CTA's shared memory may be written only once every CTA of the cluster has started: each announces itself
+  // here, and the epilogue warps wait for the whole cluster before their first remote store.
+  cluster_arrive_relaxed();
   bool have_acc = false;
 
   if (warp == 0) {
@@ -882,6 +892,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     const uint32_t row_in_tile = lane_base + lane;
     const uint32_t half = (warp - 2) >> 2;
     constexpr uint32_t kHalf = BN / 2;
+    cluster_wait();
     have_acc = mbar_wait(acc_full, 0, kWatchAccFull, abort_flag);
     if (have_acc) {
       tc_fence_after();
@@ -902,6 +913,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         }
       }
     }
+  }
+  if (warp < 2) {
+    __syncwarp();
+    cluster_wait();
   }
   // Every partial has landed in its owner's shared memory.
   cluster_sync_all();
@@ -1530,6 +1545,34 @@ static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint
   if (tiles128 >= uint64_t(sm_count()) / 2) return launch_rowmajor<128, 5, true>(a, lda, w_t, ldw, p, st);
   return launch_rowmajor<64, 8>(a, lda, w_t, ldw, p, st);
 }
+
+// ---------------------------------------------------------------------------------------------------------------
+// Failure-detection probe: one bounded mbarrier wait that nothing completes unless asked to. It exercises, on the
+// device, the path every pipeline wait takes when a copy or an MMA never arrives: the wait gives up after its limit,
+// records a watchdog code, and the kernel returns, leaving the context usable.
+// ---------------------------------------------------------------------------------------------------------------
+
+namespace tempo {
+
+__global__ void wait_probe_kernel(uint32_t arrive, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (arrive) mbar_arrive(&bar);
+    mbar_wait_for(&bar, 0, kWatchProbe, nullptr, limit_ns);
+  }
+}
+
+tempo_status launch_wait_probe(uint32_t arrive, uint64_t limit_ns, cudaStream_t stream) {
+  wait_probe_kernel<<<1, 32, 0, stream>>>(arrive, limit_ns);
+  return check_launch("wait_probe_kernel");
+}
+
+}  // namespace tempo
 
 extern "C" tempo_status tempo_block_gemm(const void* activations, const void* weights, void* drain, const void* bias,
                                          uint32_t depth, uint32_t columns, uint32_t activate, void* stream) {

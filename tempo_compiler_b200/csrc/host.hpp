@@ -36,6 +36,10 @@ int sm_count();
 // Opts a kernel into more than 48 KB of dynamic shared memory, once per device.
 tempo_status set_smem(const void* kernel, int bytes);
 
+// The failure-detection probe (gemm.cu): one CTA waits on an mbarrier that completes only if `arrive` is non-zero,
+// giving up after `limit_ns` with the watchdog code the runtime reports.
+tempo_status launch_wait_probe(uint32_t arrive, uint64_t limit_ns, cudaStream_t stream);
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Whether a grid of `ctas` fits on the GPU at once with `per_sm` resident per SM. A kernel whose grid does lets its

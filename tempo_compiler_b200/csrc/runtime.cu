@@ -366,6 +366,19 @@ extern "C" tempo_status tempo_sync(double timeout_s) {
   return sync_stream(stream, timeout_s);
 }
 
+extern "C" tempo_status tempo_wait_probe(uint32_t arrive, uint64_t limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > 10000000000ull)
+    return fail(TEMPO_ERR_VALUE, "tempo_wait_probe: the limit must be in (0, 10 s], got %llu ns",
+                (unsigned long long)limit_ns);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (s == nullptr) {
+    std::lock_guard<std::mutex> lock(g_arena.mu);
+    if (g_arena.stream == nullptr) return fail(TEMPO_ERR_STATE, "tempo_wait_probe: no device is open");
+    s = g_arena.stream;
+  }
+  return launch_wait_probe(arrive, limit_ns, s);
+}
+
 extern "C" tempo_status tempo_host_alloc(void** ptr, uint64_t nbytes) {
   if (nbytes == 0) return fail(TEMPO_ERR_VALUE, "tempo_host_alloc: zero bytes");
   void* p = nullptr;

@@ -24,6 +24,7 @@ Sequences in one batch share one prompt length.
 
 from __future__ import annotations
 
+import dataclasses
 import math
 from dataclasses import dataclass
 
@@ -103,10 +104,14 @@ class Engine:
         if not torch.cuda.is_available():
             raise RuntimeError("the B200 engine needs a CUDA device; there is no CPU path")
         self.device = torch.device(device)
+        # the vocabulary and the learned position table are whatever the weights hold
+        shape = dataclasses.replace(shape, layers=len(layers), vocab=int(shared["wte"].shape[0]),
+                                    positions=int(shared["wpe"].shape[0]))
         self.shape = shape
         self.batch, self.prompt, self.capacity = batch, prompt, capacity
-        if prompt > shape.positions or capacity > shape.positions + 1024:
-            raise ValueError(f"prompt {prompt} / capacity {capacity} exceed the model's {shape.positions} positions")
+        if not 0 < prompt <= capacity <= shape.positions:
+            raise ValueError(f"prompt {prompt} and capacity {capacity} must satisfy 0 < prompt <= capacity <= "
+                             f"{shape.positions}, the model's learned positions")
         width, heads = shape.width, shape.heads
         scale = np.ones(3 * width, dtype=np.float32)
         scale[:width] = 1.0 / math.sqrt(width // heads)

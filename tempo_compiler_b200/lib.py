@@ -50,6 +50,7 @@ _SIGNATURES = {
     "tempo_last_error": [ctypes.c_char_p, _u64],
     "tempo_stats": [ctypes.POINTER(_u64), ctypes.POINTER(_u64)],
     "tempo_watchdog": [ctypes.POINTER(_i32)],
+    "tempo_wait_probe": [_u32, _u64, _vp],
     "tempo_block_gemm": [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp],
     "tempo_block_add": [_vp, _vp, _vp, _u32, _u32, _vp],
     "tempo_block_layernorm": [_vp, _vp, _vp, _u32, _vp],

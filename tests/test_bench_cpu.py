@@ -55,7 +55,8 @@ def _reference_arm(extra_env: dict | None = None):
     env = dict(os.environ, **(extra_env or {}))
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     done = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--impl", "reference", "--steps", "1",
-                           "--warmup", "1", "--cpu-prompt", "16", "--cpu-decode", "1"],
+                           "--warmup", "1", "--cpu-prompt", "16", "--cpu-decode", "1", "--prompt", "16",
+                           "--decode", "4"],
                           capture_output=True, text=True, timeout=600, env=env, cwd=root)
     assert done.returncode == 0, done.stderr[-2000:]
     lines = [line for line in done.stdout.splitlines() if line.startswith("{")]
@@ -77,7 +78,9 @@ def test_reference_arm_prints_one_contract_line() -> None:
     assert line["higher_is_better"] is True and line["steps"] == 1 and line["value"] > 0
     baseline = line["cpu_baseline"]
     assert baseline["kind"] == "port" and baseline["cores"] >= 1 and baseline["value"] == line["value"]
-    assert "16-token prefill" in baseline["sample"]
+    assert "16-token prefill" in baseline["sample"] and "extrapolated per sequence" in baseline["sample"]
+    assert baseline["host_cpus"] >= 1 and baseline["cpu_model"] and baseline["blas_threads"] >= 1
+    assert baseline["literal_full_recompute_s_per_token"] > 0
     assert line["e2e"] == {"value": line["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
 

@@ -16,12 +16,11 @@ import pytest
 from oracle import bf16 as ob
 from oracle import references as orf
 from oracle.model import CachedChain
+from tests._greedy import TIE_MARGIN, teacher_forced
 
 pytestmark = pytest.mark.gpu
 
 torch = pytest.importorskip("torch")
-
-TIE_MARGIN = 0.02
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -49,22 +48,8 @@ def test_one_block_matches_the_oracle() -> None:
 
 
 def _check_teacher_forced(layers, shared, prompt, tokens) -> int:
-    """Returns how many steps were ties; fails if the engine picked a token the oracle ranks below the margin."""
-    chain = CachedChain(layers, shared, mode="exact")
-    logits = chain.prefill(list(prompt))
-    ties = 0
-    for step, token in enumerate(tokens):
-        best = int(np.argmax(logits))
-        gap = float(logits[best] - logits[token])
-        top = np.sort(logits)[-2:]
-        if top[1] - top[0] > TIE_MARGIN:
-            assert token == best, (step, token, best, float(top[1] - top[0]))
-        else:
-            ties += 1
-            assert gap <= TIE_MARGIN, (step, gap)
-        if step + 1 < len(tokens):
-            logits = chain.step(int(token))
-    return ties
+    """Returns how many steps were near-ties; fails if the engine picked a token the oracle ranks below the margin."""
+    return teacher_forced(layers, shared, prompt, tokens, margin=TIE_MARGIN)["near_ties"]
 
 
 def test_prefill_and_decode_greedy_tokens_match_the_oracle() -> None:
@@ -148,14 +133,3 @@ def test_free_running_greedy_identity_on_a_short_decode() -> None:
         assert list(tokens) == expected, (list(tokens), expected, margins)
     else:
         _check_teacher_forced(layers, shared, ids[0], tokens)
-
-
-def test_long_prefill_first_token_matches() -> None:
-    """A 1024-token prefill (the full-context workload) picks the oracle's first token."""
-    from tempo_compiler_b200.engine import Engine
-    from tempo_compiler_b200.weights import random_gpt2, random_token_ids
-    layers, shared = random_gpt2(13)
-    ids = random_token_ids(2, 1024).astype(np.int32)[None, :]
-    engine = Engine(layers, shared, batch=1, prompt=1024, capacity=1025)
-    tokens = engine.generate(ids, 0)
-    _check_teacher_forced(layers, shared, ids[0], tokens[0])

@@ -3,9 +3,11 @@
 tempo_lm_head_argmax_noalloc serves callers that may not allocate device memory (a plugin host that owns every device
 byte, or a loop that cannot afford cudaMalloc/cudaFree): it keeps the partials between its two kernels in an array
 compiled into the library instead of a caller buffer. This test holds it to the allocating path (tempo_gemm in argmax
-mode plus tempo_argmax_finish with caller-allocated partials) on two calls in a row, the second with fewer rows so it
-runs over the first call's leftover contents, and checks that sizes past the array's limits are refused. The tokens
-must be identical: both paths run the same kernels. The file is named to be collected last.
+mode plus tempo_argmax_finish with caller-allocated partials) on calls in a row with fewer rows each time, so every
+call after the first runs over the previous call's leftover contents: 300 and 17 rows take the tensor-core argmax
+GEMM, 8 rows and 1 row the CUDA-core GEMV argmax kernel, which writes the partials with its own kernel. It also
+checks that sizes past the array's limits are refused. The tokens must be identical: both paths run the same
+kernels. The file is named to be collected last.
 """
 
 from __future__ import annotations
@@ -40,7 +42,7 @@ def test_noalloc_lm_head_argmax_matches_the_allocating_path() -> None:
     width, vocab = 768, 50257
     generator = torch.Generator(device="cuda").manual_seed(77)
     embedding = (torch.randn((vocab, width), generator=generator, device="cuda") * 0.02).to(torch.bfloat16)
-    for rows in (300, 17):
+    for rows in (300, 17, 8, 1):
         hidden = torch.randn((rows, width), generator=generator, device="cuda").to(torch.bfloat16)
         ids = torch.full((rows,), -1, dtype=torch.int32, device="cuda")
         status = library.tempo_lm_head_argmax_noalloc(hidden.data_ptr(), width, embedding.data_ptr(), width, rows,
