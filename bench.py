@@ -54,6 +54,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--fuse-small-norms", choices=["auto", "on", "off"], default="auto",
                    help="decode groups of at most 8 sequences normalise inside their projections (default: the "
                         "engine's choice)")
+    p.add_argument("--persistent-decode", choices=["auto", "on", "off"], default="auto",
+                   help="decode steps of at most 8 sequences as one persistent kernel (default: the engine's choice)")
     p.add_argument("--decode-groups", type=int, default=None,
                    help="independent sequence groups per decode step, one CUDA stream each (default: the engine's)")
     return p.parse_args()
@@ -353,7 +355,8 @@ def b200_arm(args) -> int:
     engine = Engine(layers, shared, batch=per_rank, prompt=args.prompt, capacity=args.prompt + args.decode,
                     device=device, decode_groups=args.decode_groups,
                     fold_layernorms=None if args.fold_layernorms == "auto" else args.fold_layernorms == "on",
-                    fuse_small_norms=None if args.fuse_small_norms == "auto" else args.fuse_small_norms == "on")
+                    fuse_small_norms=None if args.fuse_small_norms == "auto" else args.fuse_small_norms == "on",
+                    persistent_decode=None if args.persistent_decode == "auto" else args.persistent_decode == "on")
     ids_dev = torch.from_numpy(ids).to(device)
     graph = not args.no_graph
 
@@ -428,11 +431,13 @@ def b200_arm(args) -> int:
                 "data": "synthetic (seeded uniform token ids, random-init weights ~N(0,0.02))",
                 "config": {**workload(args), "decode_groups_per_gpu": len(engine.decode_groups),
                            "layernorms_folded_in_decode": engine.fold_layernorms,
-                           "layernorms_inside_small_decode_projections": engine.fuse_small_norms},
+                           "layernorms_inside_small_decode_projections": engine.fuse_small_norms,
+                           "persistent_decode_step": engine.persistent_decode},
                 "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches_per_step * args.steps * world,
                 "clocks": clock_info, "roofline": roof, "gemm_roofline": gemm_roof,
-                "phases_ms_rank0": {"prefill": prefill_ms, "decode": decode_ms},
+                "phases_ms_rank0": {"prefill": prefill_ms, "decode": decode_ms,
+                                    "decode_ms_per_step": decode_ms / max(1, args.decode)},
                 "decode_graph": graph, "watchdog": watchdog,
                 "tokens_checksum": int(all_tokens.to(torch.int64).sum().item()),
                 "tokens_checksums_of_repeats": [int(r.to(torch.int64).sum().item()) for r in runs],

@@ -265,6 +265,57 @@ tempo_status tempo_lm_head_argmax_noalloc(const void* hidden, uint32_t ld_hidden
                                           uint32_t ld_embedding, uint32_t rows, uint32_t vocab, uint32_t width,
                                           int32_t* ids, void* stream);
 
+/* One greedy decode step of 1 to 8 sequences as a single persistent kernel (one CTA per SM, launched cooperatively,
+ * grid-wide barriers between its phases), replacing the kernel-per-op step of the reference's decode loop
+ * (board_package/gpt2_inference.py:865-889, decode_block :775-797, the host LM head :915-938): embedding, then per
+ * layer LayerNorm 1 + QKV + cache store, attention over each sequence's cache, out-projection + residual,
+ * LayerNorm 2 + FC + GELU, second projection + residual; then the final LayerNorm and the tied LM head's argmax.
+ * Tokens equal the kernel-per-op path's bit for bit (same per-element arithmetic). Row r consumes ids[r] at
+ * positions[r]; the step writes its pick to ids[r] and, when tokens_out is not NULL, to
+ * tokens_out[r * out_stride + positions[r] + index_offset] (if inside the row), then advances positions[r].
+ * Weights are [out, in] BF16 (K contiguous), the query rows and bias of w_qkv / b_qkv pre-scaled by 1/sqrt(64); caches
+ * are [rows][heads][capacity][64] BF16. `workspace` (tempo_decode_step_workspace bytes, 256-byte aligned) must be
+ * zero before the first step and is then left consistent by every step; one workspace serves one stream. A grid
+ * barrier that waits past its bounded time ends the kernel with watchdog code 7 (reported by tempo_sync /
+ * tempo_watchdog) and leaves the workspace unusable until it is zeroed again. */
+typedef struct tempo_decode_layer {
+  const void* ln1_gamma;
+  const void* ln1_beta;
+  const void* w_qkv;     /* [3 width, width] */
+  const void* b_qkv;     /* [3 width] */
+  const void* w_proj;    /* [width, width] */
+  const void* b_proj;
+  const void* ln2_gamma;
+  const void* ln2_beta;
+  const void* w_fc;      /* [4 width, width] */
+  const void* b_fc;
+  const void* w_out;     /* [width, 4 width] */
+  const void* b_out;
+  void* k_cache;         /* [rows][heads][capacity][64] */
+  void* v_cache;
+} tempo_decode_layer;
+
+typedef struct tempo_decode_step_args {
+  uint32_t layers, rows, width, heads, vocab, max_positions, capacity;
+  float epsilon;
+  const tempo_decode_layer* layer;  /* `layers` entries, read on the host at each call */
+  const void* wte;                  /* [vocab, width], also the LM head */
+  const void* wpe;                  /* [max_positions, width] */
+  const void* lnf_gamma;
+  const void* lnf_beta;
+  int32_t* ids;
+  int32_t* positions;
+  int32_t* tokens_out;
+  uint32_t out_stride;
+  int32_t index_offset;
+  void* workspace;
+  uint64_t workspace_bytes;
+} tempo_decode_step_args;
+
+tempo_status tempo_decode_step_workspace(uint32_t rows, uint32_t width, uint32_t heads, uint32_t vocab,
+                                         uint64_t* bytes);
+tempo_status tempo_decode_step(const tempo_decode_step_args* args, void* stream);
+
 /* Calibration (no counterpart in the reference): reads `bytes` (rounded down to whole groups of 16-byte words per
  * thread) from `src` with streaming loads and writes one 16-byte word per thread into `sink`, which holds
  * tempo_stream_read_threads() words. Its rate is the HBM read ceiling the bandwidth-bound kernels are measured against. */

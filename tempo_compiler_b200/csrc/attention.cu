@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "decode_math.cuh"
 #include "host.hpp"
 
 namespace tempo {
@@ -15,7 +16,7 @@ TEMPO_WATCHDOG_READER(watchdog_attention)
 
 namespace {
 
-constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLog2e = kDecodeLog2e;
 
 // A 16-byte load of streamed cache data that allocates no L1 line: each key and value is read exactly once, and the
 // SM's L1 may be small when a kernel with a large shared-memory carveout shares the SM.
@@ -25,76 +26,6 @@ __device__ __forceinline__ uint4 ld_stream(const uint4* ptr) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(ptr));
   return v;
-}
-
-// ---------------------------------------------------------------------------------------------------------------
-// Decode
-// ---------------------------------------------------------------------------------------------------------------
-
-__device__ __forceinline__ void load8(const uint4& w, float (&f)[8]) {
-  f[0] = bf16_lo(w.x); f[1] = bf16_hi(w.x); f[2] = bf16_lo(w.y); f[3] = bf16_hi(w.y);
-  f[4] = bf16_lo(w.z); f[5] = bf16_hi(w.z); f[6] = bf16_lo(w.w); f[7] = bf16_hi(w.w);
-}
-
-// Online-softmax state of one lane group (8 lanes x 8 dims = one head).
-struct DecodeState {
-  float m, l, acc[8];
-};
-
-// Folds KI keys (scores already in the log2 domain, -inf when absent) into the state.
-template <int KI>
-__device__ __forceinline__ void fold(DecodeState& st, const float (&sc)[KI], const uint4 (&vv)[KI]) {
-  float mb = sc[0];
-#pragma unroll
-  for (int i = 1; i < KI; ++i) mb = fmaxf(mb, sc[i]);
-  const float m_new = fmaxf(st.m, mb);
-  if (m_new == -INFINITY) return;
-  const float corr = fast_exp2(st.m - m_new);
-  float pr[KI], psum = 0.f;
-#pragma unroll
-  for (int i = 0; i < KI; ++i) {
-    pr[i] = fast_exp2(sc[i] - m_new);
-    psum += pr[i];
-  }
-  st.l = st.l * corr + psum;
-#pragma unroll
-  for (int d = 0; d < 8; ++d) st.acc[d] *= corr;
-#pragma unroll
-  for (int i = 0; i < KI; ++i) {
-    float v[8];
-    load8(vv[i], v);
-#pragma unroll
-    for (int d = 0; d < 8; ++d) st.acc[d] = fmaf(pr[i], v[d], st.acc[d]);
-  }
-  st.m = m_new;
-}
-
-// Merges the state of lane groups `other` lanes apart (xor shuffle).
-__device__ __forceinline__ void merge_shfl(DecodeState& st, int offset) {
-  const float om = __shfl_xor_sync(0xFFFFFFFFu, st.m, offset);
-  const float ol = __shfl_xor_sync(0xFFFFFFFFu, st.l, offset);
-  float oa[8];
-#pragma unroll
-  for (int d = 0; d < 8; ++d) oa[d] = __shfl_xor_sync(0xFFFFFFFFu, st.acc[d], offset);
-  const float m_new = fmaxf(st.m, om);
-  if (m_new == -INFINITY) return;
-  const float a = fast_exp2(st.m - m_new), b = fast_exp2(om - m_new);
-  st.l = st.l * a + ol * b;
-#pragma unroll
-  for (int d = 0; d < 8; ++d) st.acc[d] = st.acc[d] * a + oa[d] * b;
-  st.m = m_new;
-}
-
-__device__ __forceinline__ float group_dot(const float (&q)[8], const uint4& k) {
-  float kf[8];
-  load8(k, kf);
-  float s = 0.f;
-#pragma unroll
-  for (int d = 0; d < 8; ++d) s = fmaf(q[d], kf[d], s);
-  s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);
-  s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);
-  s += __shfl_xor_sync(0xFFFFFFFFu, s, 4);
-  return s;
 }
 
 // Native decode over the [seq][head][capacity][64] caches. A cluster of `chunks` CTAs (4 warps each) serves one
@@ -131,9 +62,8 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* _
   const uint32_t g = lane >> 3, li = lane & 7u;
   const uint32_t width = heads * 64;
   const int32_t len = max(0, min(lengths[s] + length_offset, int32_t(capacity)));
-  const int32_t per = ((len + int32_t(chunks) - 1) / int32_t(chunks) + 31) & ~31;
-  const int32_t k_begin = min(len, int32_t(chunk) * per);
-  const int32_t k_end = min(len, k_begin + per);
+  int32_t k_begin, k_end;
+  decode_chunk_range(len, chunks, chunk, k_begin, k_end);
   float q[8];
   load8(reinterpret_cast<const uint4*>(qkv + size_t(s) * 3 * width + h * 64)[li], q);
 #pragma unroll
@@ -141,31 +71,8 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* _
   const uint4* kb4 = reinterpret_cast<const uint4*>(k_cache + (size_t(s) * heads + h) * capacity * 64);
   const uint4* vb4 = reinterpret_cast<const uint4*>(v_cache + (size_t(s) * heads + h) * capacity * 64);
   DecodeState st;
-  st.m = -INFINITY;
-  st.l = 0.f;
-#pragma unroll
-  for (int d = 0; d < 8; ++d) st.acc[d] = 0.f;
-  for (int32_t base = k_begin + int32_t(warp) * 4 * KI; base < k_end; base += 16 * KI) {
-    uint4 kk[KI], vv[KI];
-#pragma unroll
-    for (int i = 0; i < KI; ++i) {
-      const int32_t key = base + i * 4 + int32_t(g);
-      if (key < k_end) {
-        kk[i] = ld_stream(kb4 + size_t(key) * 8 + li);
-        vv[i] = ld_stream(vb4 + size_t(key) * 8 + li);
-      } else {
-        kk[i] = make_uint4(0, 0, 0, 0);
-        vv[i] = make_uint4(0, 0, 0, 0);
-      }
-    }
-    float sc[KI];
-#pragma unroll
-    for (int i = 0; i < KI; ++i) {
-      const float v = group_dot(q, kk[i]);
-      sc[i] = (base + i * 4 + int32_t(g) < k_end) ? v : -INFINITY;
-    }
-    fold<KI>(st, sc, vv);
-  }
+  decode_state_init(st);
+  decode_stretch<KI>(st, q, kb4, vb4, k_begin, k_end, warp, g, li, [](const uint4* ptr) { return ld_stream(ptr); });
   // A grid of several waves lets the next kernel start its prologue only now: a trigger at entry would let that
   // kernel's CTAs take SM resources while later waves of this grid still wait to be scheduled.
   if (!early) pdl_launch_dependents();
@@ -181,16 +88,7 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* _
   __syncthreads();
   const uint32_t d = threadIdx.x;
   float m = -INFINITY, l = 0.f, a = 0.f;
-  if (d < 64) {
-    for (int w = 0; w < 4; ++w) m = fmaxf(m, sm_m[w]);
-    if (m != -INFINITY) {
-      for (int w = 0; w < 4; ++w) {
-        const float f = fast_exp2(sm_m[w] - m);
-        l += sm_l[w] * f;
-        a += sm_acc[w][d] * f;
-      }
-    }
-  }
+  if (d < 64) merge_warps(sm_m, sm_l, sm_acc, d, m, l, a);
   if (chunks == 1) {
     if (d < 64) out[size_t(s) * width + h * 64 + d] = float_to_bf16(l > 0.f ? a / l : 0.f);
     return;
@@ -206,19 +104,9 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* _
     }
   }
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-  if (chunk == 0 && d < 64) {
-    float mm = -INFINITY;
-    for (uint32_t c = 0; c < chunks; ++c) mm = fmaxf(mm, part[c][0]);
-    float ll = 0.f, aa = 0.f;
-    if (mm != -INFINITY) {
-      for (uint32_t c = 0; c < chunks; ++c) {
-        const float f = fast_exp2(part[c][0] - mm);
-        ll += part[c][1] * f;
-        aa += part[c][2 + d] * f;
-      }
-    }
-    out[size_t(s) * width + h * 64 + d] = float_to_bf16(ll > 0.f ? aa / ll : 0.f);
-  }
+  if (chunk == 0 && d < 64)
+    out[size_t(s) * width + h * 64 + d] =
+        float_to_bf16(merge_chunks(&part[0][0], 66, chunks, d, [](const float* f) { return *f; }));
 }
 
 // Packed drop-in decode: CTA per (head, group of 4 query rows); warp = one query row over all `keys` keys, scores

@@ -428,12 +428,18 @@ __device__ __forceinline__ float ln_apply(float x, float mean, float scale, floa
 
 // One row's LayerNorm by one warp: lane l holds the row's 16-byte chunks l, l + 32, ... (up to CPL of them, `features`
 // / 8 in all); mean, centred variance, rsqrt(var + epsilon), then (x - mean) rstd gamma + beta rounded to BF16, chunk
-// c handed to store(c, word) (layernorm_row: into `orow`, global or shared memory). The standalone LayerNorm and the small-M projections that normalise their own
+// c handed to store(c, word) (layernorm_row: into `orow`, global or shared memory); gamma and beta are read with
+// load (default: the read-only path). The standalone LayerNorm and the small-M projections that normalise their own
 // input share it, so both produce the same bits; a larger CPL than needed only skips chunks, in the same order.
-template <int CPL, typename Store>
+// Reads 16 bytes of read-only data (the LayerNorm's gamma and beta) through the read-only path.
+struct ReadOnlyLoad {
+  __device__ __forceinline__ uint4 operator()(const uint4* p) const { return __ldg(p); }
+};
+
+template <int CPL, typename Store, typename Load = ReadOnlyLoad>
 __device__ __forceinline__ void layernorm_row_to(const uint16_t* __restrict__ xr, const uint16_t* __restrict__ gamma,
                                                  const uint16_t* __restrict__ beta, uint32_t features, float epsilon,
-                                                 Store store) {
+                                                 Store store, Load load = Load()) {
   const uint32_t lane = lane_id();
   const uint32_t chunks = features / 8;
   float v[CPL][8];
@@ -463,8 +469,8 @@ __device__ __forceinline__ void layernorm_row_to(const uint16_t* __restrict__ xr
     const uint32_t c = lane + 32u * i;
     if (c < chunks) {
       float g[8], b[8];
-      unpack8(__ldg(reinterpret_cast<const uint4*>(gamma + c * 8)), g);
-      unpack8(__ldg(reinterpret_cast<const uint4*>(beta + c * 8)), b);
+      unpack8(load(reinterpret_cast<const uint4*>(gamma + c * 8)), g);
+      unpack8(load(reinterpret_cast<const uint4*>(beta + c * 8)), b);
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[i][j] = ln_apply(v[i][j], mean, scale, g[j], b[j]);
       store(c, pack8(v[i]));

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "decode_math.cuh"
 #include "host.hpp"
 
 namespace tempo {
@@ -36,57 +37,6 @@ constexpr uint32_t kNormMaxK = 1024;  // rows a warp normalises from registers: 
 
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
-
-// Dot products of CP weight rows (columns n0 .. n0 + CP - 1) with every activation row, summed over the warp into
-// acc[c][r]. Lane l covers the 16-byte chunks l, l + 32, ... of the contraction; each pass first issues all of its
-// CP x KCH weight loads, then does the arithmetic, so a lane keeps up to CP x KCH loads in flight (the memory-level
-// parallelism the HBM needs at a handful of rows), and passes repeat while chunks remain.
-template <int M, int KCH, int CP>
-__device__ __forceinline__ void dot_columns(const GemvParams& p, const uint16_t* a_smem, uint32_t n0,
-                                            float (&acc)[CP][M]) {
-  const uint32_t lane = lane_id();
-#pragma unroll
-  for (int c = 0; c < CP; ++c)
-#pragma unroll
-    for (int r = 0; r < M; ++r) acc[c][r] = 0.f;
-  const uint32_t chunks = p.k / 8;
-  for (uint32_t base = 0; base < chunks; base += 32 * KCH) {
-    uint4 wv[CP][KCH];
-#pragma unroll
-    for (int c = 0; c < CP; ++c) {
-      const uint4* row = reinterpret_cast<const uint4*>(p.w + size_t(n0 + c) * p.ldw);
-#pragma unroll
-      for (int i = 0; i < KCH; ++i) {
-        const uint32_t ch = base + lane + 32u * i;
-        wv[c][i] = (n0 + c < p.n && ch < chunks) ? __ldg(row + ch) : make_uint4(0, 0, 0, 0);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < KCH; ++i) {
-      const uint32_t ch = base + lane + 32u * i;
-      if (ch >= chunks) break;
-#pragma unroll
-      for (int r = 0; r < M; ++r) {
-        if (r >= int(p.m)) break;
-        float av[8];
-        unpack8(*reinterpret_cast<const uint4*>(a_smem + size_t(r) * p.k + ch * 8), av);
-#pragma unroll
-        for (int c = 0; c < CP; ++c) {
-          float wf[8];
-          unpack8(wv[c][i], wf);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[c][r] = fmaf(av[j], wf[j], acc[c][r]);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int c = 0; c < CP; ++c)
-#pragma unroll
-    for (int r = 0; r < M; ++r)
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc[c][r] += __shfl_xor_sync(0xFFFFFFFFu, acc[c][r], o);
 }
 
 // One warp per output column (CP = 1), or, in argmax mode, 32 columns of the block's 256-column tile per warp taken
@@ -132,7 +82,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_kernel(GemvParams p) {
     const uint32_t n0 = first + c0;
     if (n0 >= p.n) break;
     float acc[CP][M];
-    dot_columns<M, KCH, CP>(p, a_smem, n0, acc);
+    dot_columns<M, KCH, CP>(p.w, p.ldw, p.n, p.k, p.m, a_smem, n0, acc);
     if (argmax) {
 #pragma unroll
       for (int c = 0; c < CP; ++c)

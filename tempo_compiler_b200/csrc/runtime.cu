@@ -26,6 +26,7 @@ namespace tempo {
 int watchdog_gemm();
 int watchdog_attention();
 int watchdog_prefill();
+int watchdog_decode_step();
 
 // ---------------------------------------------------------------------------------------------------------------
 // Errors and shared host helpers
@@ -164,7 +165,9 @@ int read_watchdogs(int* gemm, int* decode, int* prefill) {
   *gemm = watchdog_gemm();
   *decode = watchdog_attention();
   *prefill = watchdog_prefill();
-  if (*gemm < 0 || *decode < 0 || *prefill < 0) return -1;
+  const int step = watchdog_decode_step();
+  if (*gemm < 0 || *decode < 0 || *prefill < 0 || step < 0) return -1;
+  if (*decode == 0) *decode = step;
   return *gemm != 0 ? *gemm : (*decode != 0 ? *decode : *prefill);
 }
 

@@ -34,6 +34,28 @@ _lib: ctypes.CDLL | None = None
 _u32, _u64, _i32, _i64, _f32, _f64 = (ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int32, ctypes.c_int64,
                                        ctypes.c_float, ctypes.c_double)
 _vp = ctypes.c_void_p
+
+
+class DecodeLayer(ctypes.Structure):
+    """tempo_decode_layer (include/tempo_b200.h): one block's device operands for the persistent decode step."""
+
+    _fields_ = [(name, ctypes.c_void_p) for name in (
+        "ln1_gamma", "ln1_beta", "w_qkv", "b_qkv", "w_proj", "b_proj", "ln2_gamma", "ln2_beta", "w_fc", "b_fc",
+        "w_out", "b_out", "k_cache", "v_cache")]
+
+
+class DecodeStepArgs(ctypes.Structure):
+    """tempo_decode_step_args (include/tempo_b200.h)."""
+
+    _fields_ = [("layers", ctypes.c_uint32), ("rows", ctypes.c_uint32), ("width", ctypes.c_uint32),
+                ("heads", ctypes.c_uint32), ("vocab", ctypes.c_uint32), ("max_positions", ctypes.c_uint32),
+                ("capacity", ctypes.c_uint32), ("epsilon", ctypes.c_float), ("layer", ctypes.POINTER(DecodeLayer)),
+                ("wte", ctypes.c_void_p), ("wpe", ctypes.c_void_p), ("lnf_gamma", ctypes.c_void_p),
+                ("lnf_beta", ctypes.c_void_p), ("ids", ctypes.c_void_p), ("positions", ctypes.c_void_p),
+                ("tokens_out", ctypes.c_void_p), ("out_stride", ctypes.c_uint32), ("index_offset", ctypes.c_int32),
+                ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64)]
+
+
 _SIGNATURES = {
     "tempo_open": [ctypes.c_int, _u64],
     "tempo_close": [],
@@ -71,6 +93,8 @@ _SIGNATURES = {
     "tempo_lm_head_argmax_noalloc": [_vp, _u32, _vp, _u32, _u32, _u32, _u32, _vp, _vp],
     "tempo_gemm_norm": [_vp, _u32, _vp, _vp, _f32, _vp, _u32, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp, _vp,
                         _vp, _u32, _u32, _u32, _vp, _vp],
+    "tempo_decode_step_workspace": [_u32, _u32, _u32, _u32, ctypes.POINTER(_u64)],
+    "tempo_decode_step": [ctypes.POINTER(DecodeStepArgs), _vp],
     "tempo_stream_read_threads": [ctypes.POINTER(_u32)],
     "tempo_stream_read": [_vp, _u64, _vp, _vp],
 }

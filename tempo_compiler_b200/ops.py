@@ -150,6 +150,17 @@ def gemm_argmax(a: torch.Tensor, w_t: torch.Tensor, part_val: torch.Tensor, part
               part_val.data_ptr(), part_idx.data_ptr(), _stream())
 
 
+def decode_step_workspace_bytes(rows: int, width: int, heads: int, vocab: int) -> int:
+    size = ctypes.c_uint64()
+    _lib.call("tempo_decode_step_workspace", rows, width, heads, vocab, ctypes.byref(size))
+    return int(size.value)
+
+
+def decode_step(args: "_lib.DecodeStepArgs") -> None:
+    """One persistent decode step (tempo_decode_step) with prepared arguments, on the current stream."""
+    _launch("tempo_decode_step", ctypes.byref(args), _stream())
+
+
 def argmax_finish(part_val: torch.Tensor, part_idx: torch.Tensor, ids: torch.Tensor, *,
                   tokens_out: torch.Tensor | None = None, positions: torch.Tensor | None = None,
                   index_offset: int = 0, advance: int = 0) -> None:
