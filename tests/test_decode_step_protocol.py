@@ -1,13 +1,17 @@
-"""CPU model check of the persistent decode step's grid barrier (`csrc/decode_step.cu`, `grid_barrier`).
+"""CPU model check of the persistent decode step's grid barrier (`csrc/decode_step.cu`, `GridBarrier`).
 
-Every CTA's thread 0 reads the generation word, arrives on the arrival counter, and either (the last to arrive)
-resets the counter and then publishes generation + 1, or spins until the generation word moves. The model runs that
-protocol for several CTAs through several consecutive barriers under random schedules, each read, atomic and store
-one step, and checks that no CTA leaves a barrier before every CTA has arrived at it (so whatever a CTA wrote before
-arriving is complete when any CTA passes) and that the counter is back at zero whenever a barrier opens. It also
-models the last-CTA pattern that ends the step (every CTA counts itself out after writing its LM-head partials; the
-last one alone reduces them). Two planted mistakes are caught: the generation read after the arrival, and the
-counter reset after the generation is published.
+The barrier is a 64-bit arrival counter that only grows. At entry every CTA's thread 0 reads the counter and rounds it
+down to a multiple of the grid size (the launch's base); barrier b of the launch (b = 1, 2, ...) is one arrival (a
+release add) followed by a poll until the counter reaches base + b x grid. The model runs whole launches back to back,
+as a stream runs them (launch L + 1 starts once every CTA of launch L has returned), with the CTAs of a launch starting
+at random moments, so a slow CTA may read the counter after fast ones have arrived at the first barrier. It checks
+that no CTA leaves a barrier before every CTA has arrived at it, that every launch ends, and that the counter ends at
+launches x barriers x grid. It also models the last-CTA pattern that ends the step (every CTA counts itself out after
+writing its LM-head partials; the last one alone reduces them and resets the count).
+
+Planted mistakes are caught: a base taken without rounding down (the slow CTA then waits for an arrival that never
+comes), a target one barrier short (a CTA leaves before the others arrive), and a launch in which one CTA skips the
+last barrier (the next launch's base is then wrong).
 """
 
 from __future__ import annotations
@@ -19,71 +23,66 @@ import pytest
 from _protocol import Violation, check, run
 
 
-class Memory:
+class Counter:
     def __init__(self) -> None:
-        self.count = 0
-        self.generation = 0
+        self.value = 0
 
 
-def cta(mem: Memory, ctas: int, index: int, barriers: int, arrived: list[set[int]], passed: list[set[int]],
-        read_late: bool = False, reset_late: bool = False):
-    for b in range(barriers):
-        if not read_late:
-            gen = mem.generation
-            yield
+def cta(counter: Counter, grid: int, index: int, barriers: int, arrived: list[set[int]], passed: list[set[int]],
+        no_round: bool = False, short: bool = False, skip_last: bool = False):
+    for _ in range(random.Random(index).randrange(4)):
+        yield                                            # a CTA starts late
+    seen = counter.value
+    base = seen if no_round else (seen // grid) * grid
+    yield
+    for b in range(1, barriers + 1):
+        if skip_last and index == 0 and b == barriers:
+            return
         arrived[b].add(index)
-        old = mem.count
-        mem.count += 1                       # atomicAdd: one indivisible step
+        counter.value += 1                               # red.release.add: one indivisible step
         yield
-        if read_late:
-            gen = mem.generation
+        target = base + (b - 1 if short else b) * grid
+        while counter.value < target:
             yield
-        if old == ctas - 1:
-            if reset_late:
-                mem.generation = gen + 1
-                yield
-                mem.count = 0
-                yield
-            else:
-                mem.count = 0
-                yield
-                mem.generation = gen + 1     # st.release after the reset
-                yield
-        else:
-            while mem.generation == gen:
-                yield
-        check(arrived[b] == set(range(ctas)), f"CTA {index} left barrier {b} before every CTA arrived")
+        check(arrived[b] == set(range(grid)), f"CTA {index} left barrier {b} before every CTA arrived")
         passed[b].add(index)
         yield
 
 
-def schedule(ctas: int, barriers: int, seed: int, **mistake) -> None:
-    mem = Memory()
-    arrived = [set() for _ in range(barriers)]
-    passed = [set() for _ in range(barriers)]
-    roles = {f"cta{i}": cta(mem, ctas, i, barriers, arrived, passed, **mistake) for i in range(ctas)}
-    run(roles, [], random.Random(seed), limit=200000)
-    check(all(p == set(range(ctas)) for p in passed), "a CTA never passed a barrier")
-    check(mem.count == 0, "the arrival counter is not back at zero")
-    check(mem.generation == barriers, "the generation did not advance once per barrier")
+def launches(grid: int, barriers: int, count: int, seed: int, **mistake) -> None:
+    counter = Counter()
+    rng = random.Random(seed)
+    for launch in range(count):
+        arrived = [set() for _ in range(barriers + 1)]
+        passed = [set() for _ in range(barriers + 1)]
+        roles = {f"cta{i}": cta(counter, grid, i, barriers, arrived, passed, **mistake) for i in range(grid)}
+        run(roles, [], rng, limit=200000)
+        check(all(passed[b] == set(range(grid)) for b in range(1, barriers + 1)),
+              f"launch {launch}: a CTA never passed a barrier")
+    check(counter.value == count * barriers * grid, "the counter does not count every arrival")
 
 
 @pytest.mark.parametrize("seed", range(60))
-def test_grid_barrier_holds_under_random_schedules(seed: int) -> None:
-    schedule(ctas=2 + seed % 7, barriers=6, seed=seed)
+def test_grid_barrier_holds_across_launches(seed: int) -> None:
+    launches(grid=2 + seed % 7, barriers=5, count=3, seed=seed)
 
 
-@pytest.mark.parametrize("seed", range(40))
-def test_reading_the_generation_after_arriving_is_caught(seed: int) -> None:
+def test_base_without_rounding_is_caught() -> None:
     with pytest.raises(Violation):
-        for extra in range(10):
-            schedule(ctas=3 + seed % 4, barriers=5, seed=seed * 31 + extra, read_late=True)
+        for seed in range(200):
+            launches(grid=4, barriers=4, count=2, seed=seed, no_round=True)
 
 
-def test_resetting_the_counter_after_publishing_is_caught() -> None:
+def test_target_one_barrier_short_is_caught() -> None:
     with pytest.raises(Violation):
-        for seed in range(400):
-            schedule(ctas=4, barriers=8, seed=seed, reset_late=True)
+        for seed in range(50):
+            launches(grid=3, barriers=4, count=1, seed=seed, short=True)
+
+
+def test_a_skipped_barrier_breaks_the_next_launch() -> None:
+    with pytest.raises(Violation):
+        for seed in range(50):
+            launches(grid=3, barriers=4, count=2, seed=seed, skip_last=True)
 
 
 def test_last_cta_reduces_only_complete_partials() -> None:
