@@ -728,12 +728,15 @@ tempo_status launch_rowmajor(const void* a, uint32_t lda, const void* w_t, uint3
 // ---------------------------------------------------------------------------------------------------------------
 // Split-K for small M (the decode projections): a cluster of SPLITS CTAs shares one 128 x BN output tile, each CTA
 // running a contiguous share of the k-blocks into its own TMEM accumulator. The FP32 partial tiles are reduced
-// through distributed shared memory: CTA r owns rows [r*128/SPLITS, (r+1)*128/SPLITS) of the tile, every CTA writes
-// its partial rows (those inside M) into the owner's shared memory, one cluster barrier, and each owner sums its rows
-// and runs the epilogue with coalesced 16-byte stores. No workspace and no atomics. The 16-byte chunks of partial row
-// r are XOR-swizzled by r % 8, so the 32 lanes of a warp, one row each, store into different banks without padding
-// (the shared memory stays within the 196 KB carveout, which leaves 60 KB of L1 to kernels sharing the SM). The ring
-// holds only as many stages as a split has k-blocks.
+// through distributed shared memory: CTA r owns rows [r*128/SPLITS, (r+1)*128/SPLITS) of the tile. Each epilogue
+// warp holds 32 rows (its TMEM lane quarter) x one half of the columns; it writes the rows it owns straight into its
+// own reduction buffer and the others into a staging tile in the (by then idle) operand ring, and sends each staged
+// piece to its owner with one bulk shared::cta -> shared::cluster copy that completes on the owner's mbarrier. The
+// owner waits for the bytes of the other SPLITS - 1 CTAs, sums the partials in rank order and runs the epilogue with
+// coalesced 16-byte stores, its bias and residual already loaded while the MMAs ran. No workspace and no atomics.
+// The 16-byte chunks of each partial row are XOR-swizzled by row % 8, so the 32 lanes of a warp, one row each, store
+// into different banks without padding (the shared memory stays within the 196 KB carveout, which leaves 60 KB of
+// L1 to kernels sharing the SM). The ring holds only as many stages as a split has k-blocks (two or more).
 // ---------------------------------------------------------------------------------------------------------------
 
 template <int BN, int SPLITS, int STAGES>
@@ -742,12 +745,22 @@ struct SplitSmem {
   static constexpr uint32_t kBBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kRowsPer = 128 / SPLITS;
-  static constexpr uint32_t kRedBytes = 128 * BN * 4;  // [SPLITS][kRowsPer][BN] FP32 partials, chunks swizzled
-  static constexpr uint32_t kBarriers = 2 * STAGES + 2;  // full, empty, acc_full, final
+  static constexpr uint32_t kHalfCols = BN / 2;  // the columns one epilogue warp holds
+  // [SPLITS source ranks][2 halves][kRowsPer rows][kHalfCols] FP32 partials: the piece one warp sends an owner is
+  // contiguous.
+  static constexpr uint32_t kRedBytes = 128 * BN * 4;
+  static constexpr uint32_t kRemoteBytes = (SPLITS - 1) * kRowsPer * BN * 4;  // what an owner receives
+  // A staging tile of 32 rows x kHalfCols per epilogue warp, in the operand ring (two stages or more).
+  static constexpr uint32_t kStagingBytes = (kEpilogueThreads / 32) * 32 * kHalfCols * 4;
+  static_assert(kStagingBytes <= 2 * kStageBytes, "split-K staging exceeds two ring stages");
+  static constexpr uint32_t kBarriers = 2 * STAGES + 3;  // full, empty, acc_full, final, red_full
   __host__ __device__ static constexpr uint32_t red_offset(uint32_t stages) { return stages * kStageBytes; }
   __host__ __device__ static constexpr uint32_t barrier_offset(uint32_t stages) { return red_offset(stages) + kRedBytes; }
   __host__ __device__ static constexpr uint32_t bytes(uint32_t stages) {
     return barrier_offset(stages) + kBarriers * 8 + 16 + 1024;
+  }
+  __host__ __device__ static constexpr uint32_t block(uint32_t src, uint32_t half) {
+    return (src * 2 + half) * kRowsPer * kHalfCols;  // in floats
   }
   static_assert(barrier_offset(STAGES) + kBarriers * 8 + 16 + 1024 <= 195 * 1024,
                 "split-K GEMM shared memory exceeds the 196 KB carveout");
@@ -770,6 +783,17 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_
                : "memory");
 }
 
+// A bulk copy from this CTA's shared memory into another CTA's of the cluster (both addresses 16-byte aligned, the
+// size a multiple of 16), completing `bytes` of transactions on the destination CTA's mbarrier.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                                     uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster),
+      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
+
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -790,14 +814,19 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t stages = p.stages;
   float* red = reinterpret_cast<float*>(smem + L::red_offset(stages));
+  float* staging = reinterpret_cast<float*>(smem);  // the operand ring, idle once the accumulator is final
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::barrier_offset(stages));
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* acc_full = bars + 2 * STAGES;
   uint64_t* final_bar = acc_full + 1;
+  uint64_t* red_full = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kBarriers);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+  constexpr uint32_t kHalfCols = L::kHalfCols;
+  constexpr uint32_t kChunks = BN / 8;  // 8-column chunks per tile row
+  constexpr uint32_t kItems = (L::kRowsPer * kChunks + kEpilogueThreads - 1) / kEpilogueThreads;
 
   const uint32_t warp = warp_id(), lane = lane_id();
   const uint32_t rank = cluster_rank();
@@ -813,6 +842,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     }
     mbar_init(acc_full, 1);
     mbar_init(final_bar, 1);
+    // Completes once the other CTAs' partial rows for this CTA have all landed.
+    mbar_init(red_full, 1);
+    mbar_arrive_expect_tx(red_full, L::kRemoteBytes);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmap_a);
@@ -827,10 +859,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_launch_dependents();
-  // Another CTA's shared memory may be written only once every CTA of the cluster has started: each announces itself
-  // here, and the epilogue warps wait for the whole cluster before their first remote store.
+  // Another CTA's shared memory (and its mbarrier) may be written only once every CTA of the cluster has started and
+  // initialised its barriers: each announces itself here, and the epilogue warps wait for the whole cluster before
+  // their first copy.
   cluster_arrive_relaxed();
-  bool have_acc = false;
 
   if (warp == 0) {
     if (elect_one()) {
@@ -863,6 +895,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       for (int s = 0; s < STAGES; ++s)
         if (used[s]) mbar_wait(&full[s], last_parity[s], kWatchFull, nullptr);
     }
+    __syncwarp();
+    cluster_wait();
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idesc = make_idesc_bf16(128, BN, 0, 0);
@@ -886,100 +920,128 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       umma_commit(final_bar);
       mbar_wait(final_bar, 0, kWatchOther, nullptr);
     }
-  } else {
-    // Phase 1: this CTA's partial rows go to their owners' shared memory.
-    const uint32_t lane_base = 32u * (warp & 3u);
-    const uint32_t row_in_tile = lane_base + lane;
-    const uint32_t half = (warp - 2) >> 2;
-    constexpr uint32_t kHalf = BN / 2;
-    cluster_wait();
-    have_acc = mbar_wait(acc_full, 0, kWatchAccFull, abort_flag);
-    if (have_acc) {
-      tc_fence_after();
-      const uint32_t owner = row_in_tile / L::kRowsPer, owned_row = row_in_tile % L::kRowsPer;
-      const uint32_t slot = rank * L::kRowsPer + owned_row;
-      const uint32_t remote = map_to_rank(smem_u32(red + size_t(slot) * BN), owner);
-      const bool inside = m_blk * 128 + row_in_tile < p.m;
-#pragma unroll 1
-      for (uint32_t c = half * kHalf; c < (half + 1) * kHalf; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (lane_base << 16) + c, r);
-        tmem_wait_ld();
-        if (inside) {
-#pragma unroll
-          for (uint32_t q = 0; q < 8; ++q)
-            st_cluster_v4(remote + (((c / 4 + q) ^ (slot & 7u)) * 16), r[q * 4], r[q * 4 + 1], r[q * 4 + 2],
-                          r[q * 4 + 3]);
-        }
-      }
-    }
-  }
-  if (warp < 2) {
     __syncwarp();
     cluster_wait();
-  }
-  // Every partial has landed in its owner's shared memory.
-  cluster_sync_all();
-  if (warp >= 2 && !*abort_flag) {
-    // Phase 2: sum the owned rows' partials, then bias / GELU / residual and 16-byte BF16 stores. The residual and
-    // the output may be the previous kernel's operands: wait for it (already finished, as the A operand was).
-    pdl_wait();
+  } else {
     const uint32_t t = threadIdx.x - 64;
-    constexpr uint32_t kChunks = BN / 8;
     const bool gelu = (p.flags & TEMPO_GEMM_GELU) != 0;
-    for (uint32_t item = t; item < L::kRowsPer * kChunks; item += kEpilogueThreads) {
+    cluster_wait();
+    // The bias and the residual of this thread's output chunks, loaded while the MMAs run. The residual (and the
+    // output) may be the previous kernel's: wait for it first (the A operand's producer has already waited).
+    pdl_wait();
+    uint4 pre_bias[kItems], pre_res[kItems];
+#pragma unroll
+    for (uint32_t i = 0; i < kItems; ++i) {
+      const uint32_t item = t + i * kEpilogueThreads;
       const uint32_t lr = item / kChunks, c8 = item % kChunks;
       const uint32_t row = m_blk * 128 + rank * L::kRowsPer + lr;
       const uint32_t col = n_blk * BN + c8 * 8;
-      if (row >= p.m || col >= p.n) continue;
-      float v[8];
+      const bool in = item < L::kRowsPer * kChunks && row < p.m && col < p.n;
+      pre_bias[i] = in && p.bias != nullptr ? __ldg(reinterpret_cast<const uint4*>(p.bias + col)) : make_uint4(0, 0, 0, 0);
+      pre_res[i] = in && p.residual != nullptr
+                       ? *reinterpret_cast<const uint4*>(p.residual + size_t(row) * p.ldr + col)
+                       : make_uint4(0, 0, 0, 0);
+    }
+
+    // Phase 1: warp (quarter q, half h) holds tile rows 32q .. 32q + 31 x columns h * BN / 2 ...; each lane's
+    // half-row goes to its owner's block [rank][h], directly if this CTA owns it, else through the warp's staging
+    // tile and one bulk copy per owner.
+    const uint32_t quarter = warp & 3u, half = (warp - 2) >> 2;
+    const uint32_t row_in_tile = 32u * quarter + lane;
+    const uint32_t owner = row_in_tile / L::kRowsPer, owned_row = row_in_tile % L::kRowsPer;
+    float* stage_rows = staging + (warp - 2) * 32 * kHalfCols;
+    float* dst_row = owner == rank ? red + L::block(rank, half) + owned_row * kHalfCols : stage_rows + lane * kHalfCols;
+    const uint32_t key = lane & 7u;  // == owned_row % 8: kRowsPer and 32 q are multiples of 8
+    const bool have_acc = mbar_wait(acc_full, 0, kWatchAccFull, abort_flag);
+    if (have_acc) {
+      tc_fence_after();
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = 0.f;
+      for (uint32_t c = 0; c < kHalfCols; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((32u * quarter) << 16) + half * kHalfCols + c, r);
+        tmem_wait_ld();
 #pragma unroll
-      for (uint32_t s = 0; s < uint32_t(SPLITS); ++s) {
-        const uint32_t slot = s * L::kRowsPer + lr;
-        const float4* row_base = reinterpret_cast<const float4*>(red + size_t(slot) * BN);
-        const float4 x = row_base[(2 * c8) ^ (slot & 7u)], y = row_base[(2 * c8 + 1) ^ (slot & 7u)];
-        v[0] += x.x; v[1] += x.y; v[2] += x.z; v[3] += x.w;
-        v[4] += y.x; v[5] += y.y; v[6] += y.z; v[7] += y.w;
-      }
-      if (p.bias != nullptr) {
-        const uint4 w = __ldg(reinterpret_cast<const uint4*>(p.bias + col));
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          v[2 * h] += bf16_lo(ws[h]);
-          v[2 * h + 1] += bf16_hi(ws[h]);
+        for (uint32_t q = 0; q < 8; ++q) {
+          float4* chunk = reinterpret_cast<float4*>(dst_row) + ((c / 4 + q) ^ key);
+          *chunk = make_float4(__uint_as_float(r[q * 4]), __uint_as_float(r[q * 4 + 1]),
+                               __uint_as_float(r[q * 4 + 2]), __uint_as_float(r[q * 4 + 3]));
         }
       }
-      if (gelu) {
-#pragma unroll
-        for (int j = 0; j < 8; j += 2) {
-          const uint32_t rounded = pack_bf16x2(v[j], v[j + 1]);
-          v[j] = bf16_lo(rounded);
-          v[j + 1] = bf16_hi(rounded);
-          gelu_erf_pair(v[j], v[j + 1]);
-        }
+      // The staged rows reach the copy engine (the async proxy) only after this fence.
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      // One piece per owner: 32 rows (SPLITS <= 4) or two pieces of 16 rows (SPLITS = 8).
+      constexpr uint32_t kPieceRows = L::kRowsPer < 32 ? L::kRowsPer : 32u;
+      if (lane % kPieceRows == 0 && owner != rank) {
+        const uint32_t bytes = kPieceRows * kHalfCols * 4;
+        const uint32_t dst = map_to_rank(smem_u32(red + L::block(rank, half) + owned_row * kHalfCols), owner);
+        bulk_copy_to_cluster(dst, smem_u32(stage_rows + lane * kHalfCols), bytes, map_to_rank(smem_u32(red_full), owner));
       }
-      if (p.residual != nullptr) {
-        const uint4 w = *reinterpret_cast<const uint4*>(p.residual + size_t(row) * p.ldr + col);
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    }
+    // This CTA's own rows are in place once every epilogue warp has passed here; the others' once red_full completes.
+    asm volatile("bar.sync 1, %0;" ::"r"(kEpilogueThreads) : "memory");
+    const bool have_all = have_acc && mbar_wait(red_full, 0, kWatchOther, abort_flag);
+
+    if (have_all && !*abort_flag) {
+      // Phase 2: sum the owned rows' partials in rank order, then bias / GELU / residual and 16-byte BF16 stores.
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          v[2 * h] += bf16_lo(ws[h]);
-          v[2 * h + 1] += bf16_hi(ws[h]);
+      for (uint32_t i = 0; i < kItems; ++i) {
+        const uint32_t item = t + i * kEpilogueThreads;
+        if (item >= L::kRowsPer * kChunks) continue;
+        const uint32_t lr = item / kChunks, c8 = item % kChunks;
+        const uint32_t row = m_blk * 128 + rank * L::kRowsPer + lr;
+        const uint32_t col = n_blk * BN + c8 * 8;
+        if (row >= p.m || col >= p.n) continue;
+        const uint32_t h = c8 / (kChunks / 2), cc = c8 % (kChunks / 2);
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = 0.f;
+#pragma unroll
+        for (uint32_t s = 0; s < uint32_t(SPLITS); ++s) {
+          const float4* row_base = reinterpret_cast<const float4*>(red + L::block(s, h) + lr * kHalfCols);
+          const float4 x = row_base[(2 * cc) ^ (lr & 7u)], y = row_base[(2 * cc + 1) ^ (lr & 7u)];
+          v[0] += x.x; v[1] += x.y; v[2] += x.z; v[3] += x.w;
+          v[4] += y.x; v[5] += y.y; v[6] += y.z; v[7] += y.w;
         }
+        if (p.bias != nullptr) {
+          const uint32_t ws[4] = {pre_bias[i].x, pre_bias[i].y, pre_bias[i].z, pre_bias[i].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            v[2 * q] += bf16_lo(ws[q]);
+            v[2 * q + 1] += bf16_hi(ws[q]);
+          }
+        }
+        if (gelu) {
+#pragma unroll
+          for (int j = 0; j < 8; j += 2) {
+            const uint32_t rounded = pack_bf16x2(v[j], v[j + 1]);
+            v[j] = bf16_lo(rounded);
+            v[j + 1] = bf16_hi(rounded);
+            gelu_erf_pair(v[j], v[j + 1]);
+          }
+        }
+        if (p.residual != nullptr) {
+          const uint32_t ws[4] = {pre_res[i].x, pre_res[i].y, pre_res[i].z, pre_res[i].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            v[2 * q] += bf16_lo(ws[q]);
+            v[2 * q + 1] += bf16_hi(ws[q]);
+          }
+        }
+        uint4 o;
+        o.x = pack_bf16x2(v[0], v[1]);
+        o.y = pack_bf16x2(v[2], v[3]);
+        o.z = pack_bf16x2(v[4], v[5]);
+        o.w = pack_bf16x2(v[6], v[7]);
+        *reinterpret_cast<uint4*>(p.out + size_t(row) * p.ldo + col) = o;
+        uint4* cache4 = reinterpret_cast<uint4*>(kv_destination(p.kv, row, col));
+        if (cache4 != nullptr) *cache4 = o;
       }
-      uint4 o;
-      o.x = pack_bf16x2(v[0], v[1]);
-      o.y = pack_bf16x2(v[2], v[3]);
-      o.z = pack_bf16x2(v[4], v[5]);
-      o.w = pack_bf16x2(v[6], v[7]);
-      *reinterpret_cast<uint4*>(p.out + size_t(row) * p.ldo + col) = o;
-      uint4* cache4 = reinterpret_cast<uint4*>(kv_destination(p.kv, row, col));
-      if (cache4 != nullptr) *cache4 = o;
     }
   }
+  // No CTA leaves (freeing the shared memory that copies read from or write into) before every CTA of the cluster
+  // has received its partials.
+  cluster_sync_all();
 
   tc_fence_before();
   __syncthreads();
@@ -1013,6 +1075,9 @@ tempo_status launch_splitk(const void* a, uint32_t lda, const void* w_t, uint32_
   p.n_tiles = (p.n + BN - 1) / BN;
   const uint32_t per_split = ((p.k + kBK - 1) / kBK + SPLITS - 1) / SPLITS;
   p.stages = per_split < uint32_t(STAGES) ? per_split : uint32_t(STAGES);
+  // The epilogue stages its outgoing partial rows in the first two ring stages.
+  if (p.stages < 2 || (p.k + kBK - 1) / kBK < 2 * SPLITS)
+    return fail(TEMPO_ERR_VALUE, "split-K GEMM needs two k-blocks or more per split (k %u, %d splits)", p.k, SPLITS);
   auto kernel = gemm_splitk_kernel<BN, SPLITS, STAGES>;
   s = set_smem(reinterpret_cast<const void*>(kernel), L::bytes(STAGES));
   if (s != TEMPO_OK) return s;
