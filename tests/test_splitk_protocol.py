@@ -5,8 +5,9 @@ of every CTA initialises its `red_full` mbarrier and announces, with its single 
 send it; every thread arrives on the cluster barrier. Each of the 8 epilogue warps (TMEM lane quarter q, column half
 h) waits for the cluster, writes the rows it owns straight into its own reduction buffer, stages the others in the
 operand ring and issues one bulk copy per remote owner, which lands after a random latency, in any order,
-completing its bytes on the owner's `red_full`. The warps of a CTA then meet on a named barrier (their own rows are in place), wait for
-`red_full`, read every partial of their rows and store the outputs; a final cluster barrier precedes the exit.
+completing its bytes on the owner's `red_full`. The warps of a CTA then meet on a named barrier (their own rows are
+in place), wait for `red_full`, read every partial of their rows and store the outputs; a final cluster barrier
+precedes the exit.
 
 Each run interleaves the CTAs' warps and the copy engine at random and checks: a copy is issued only once its
 destination CTA has started, it reads a staging tile whose CTA has not exited and writes into a CTA that has not
