@@ -217,6 +217,27 @@ tempo_status tempo_gemm_ln(const void* x, uint32_t ldx, const void* w_t_folded, 
                            uint32_t k, uint32_t flags, void* k_cache, void* v_cache, uint32_t seqs, uint32_t heads,
                            uint32_t head, uint32_t capacity, const int32_t* positions, void* stream);
 
+/* tempo_gemm whose epilogue also writes the statistics partials of the BF16 rows it stores: row_stats [m][n / 16]
+ * float pairs (mean, M2) of each 16-column chunk (M2 = sum of squared deviations from the chunk mean). N % 16 == 0,
+ * flags 0 or TEMPO_GEMM_GELU. The residual projections write them for the folded LayerNorm of the next projection. */
+tempo_status tempo_gemm_rowstats(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
+                                 const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m, uint32_t n,
+                                 uint32_t k, uint32_t flags, float* row_stats, void* stream);
+
+/* tempo_gemm_ln with mean_r and rstd_r combined from row_stats [m][k / 16] (tempo_gemm_rowstats' or
+ * tempo_row_stats' partials of x: the mean of the chunk means, M2 = sum M2_c + 16 sum (mean_c - mean)^2, each summed
+ * in a fixed order) instead of computed from x in the kernel, so the projection may split K. K % 16 == 0, K <= 1024. */
+tempo_status tempo_gemm_ln_rowstats(const void* x, uint32_t ldx, const void* w_t_folded, uint32_t ldw,
+                                    const float* colsum, const float* bias_folded, float epsilon, const float* row_stats,
+                                    void* out, uint32_t ldo, uint32_t m, uint32_t n, uint32_t k, uint32_t flags,
+                                    void* k_cache, void* v_cache, uint32_t seqs, uint32_t heads, uint32_t head,
+                                    uint32_t capacity, const int32_t* positions, void* stream);
+
+/* The statistics partials of `rows` BF16 rows of `width` (width % 16 == 0, row stride ldx % 8 == 0), in
+ * tempo_gemm_rowstats' layout: for rows no projection wrote (the embedding's). */
+tempo_status tempo_row_stats(const void* x, uint32_t ldx, uint32_t rows, uint32_t width, float* row_stats,
+                             void* stream);
+
 /* Row-wise LayerNorm of `rows` BF16 rows of `features` (features % 8 == 0, <= 4096) read `x_stride` elements apart
  * (x_stride % 8 == 0), FP32 statistics, BF16 out [rows, features]. */
 tempo_status tempo_layernorm(const void* x, uint32_t x_stride, const void* gamma, const void* beta, void* out,

@@ -143,6 +143,22 @@ __device__ __forceinline__ void gelu_erf_pair(float& a, float& b) {
   b = b * (b < 0.f ? tb : 1.0f - tb);
 }
 
+// (mean, M2) of 16 values: the mean, then the sum of squared deviations from it. The row statistics partials a
+// projection writes for the LayerNorm folded into the projection after it.
+__device__ __forceinline__ float2 chunk_stats16(const float (&w)[16]) {
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) s += w[j];
+  const float mean = s * (1.f / 16.f);
+  float m2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float d = w[j] - mean;
+    m2 = fmaf(d, d, m2);
+  }
+  return make_float2(mean, m2);
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // Shared memory addressing and mbarriers
 // ---------------------------------------------------------------------------------------------------------------

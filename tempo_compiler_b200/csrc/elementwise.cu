@@ -91,6 +91,29 @@ __global__ void layernorm_kernel(const uint16_t* __restrict__ x, uint32_t x_stri
   if (!early) pdl_launch_dependents();
 }
 
+// ---- row statistics partials: (mean, M2) of each 16-column chunk of each row, for a folded LayerNorm ----
+__global__ void row_stats_kernel(const uint16_t* __restrict__ x, uint32_t ldx, uint32_t rows, uint32_t width,
+                                 float2* __restrict__ stats, uint32_t early) {
+  if (early) pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t chunks = width / 16;
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < rows * chunks) {
+    const uint32_t r = i / chunks, c = i % chunks;
+    const uint4* src = reinterpret_cast<const uint4*>(x + size_t(r) * ldx + c * 16);
+    float lo[8], hi[8], w[16];
+    unpack8(src[0], lo);
+    unpack8(src[1], hi);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      w[j] = lo[j];
+      w[8 + j] = hi[j];
+    }
+    stats[i] = chunk_stats16(w);
+  }
+  if (!early) pdl_launch_dependents();
+}
+
 // ---- embedding gather: x[r] = round(wte[ids[r]] + wpe[pos[r]]) ----
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ positions,
                              const uint16_t* __restrict__ wte, const uint16_t* __restrict__ wpe,
@@ -230,6 +253,19 @@ extern "C" tempo_status tempo_layernorm(const void* x, uint32_t x_stride, const 
               : cpl <= 8 ? layernorm_kernel<8>
                          : layernorm_kernel<16>;
   return launch(kernel, grid, block, 0, st, 1, "layernorm_kernel", xs, x_stride, gs, bs, os, rows, features, epsilon,
+                single_wave(grid.x, 8));
+}
+
+extern "C" tempo_status tempo_row_stats(const void* x, uint32_t ldx, uint32_t rows, uint32_t width, float* stats,
+                                        void* stream) {
+  if (rows == 0 || width == 0 || width % 16 || ldx < width || ldx % 8 || !aligned16(x) || stats == nullptr ||
+      (reinterpret_cast<uintptr_t>(stats) & 7u))
+    return fail(TEMPO_ERR_VALUE, "tempo_row_stats: rows %u width %u (multiple of 16) stride %u, aligned operands", rows,
+                width, ldx);
+  const uint64_t threads = uint64_t(rows) * (width / 16);
+  const dim3 grid(uint32_t((threads + 255) / 256)), block(256);
+  return launch(row_stats_kernel, grid, block, 0, static_cast<cudaStream_t>(stream), 1, "row_stats_kernel",
+                static_cast<const uint16_t*>(x), ldx, rows, width, reinterpret_cast<float2*>(stats),
                 single_wave(grid.x, 8));
 }
 

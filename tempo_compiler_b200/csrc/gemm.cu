@@ -57,6 +57,12 @@ struct RowMajorParams {
   const float* ln_colsum;
   const float* ln_bias;
   float ln_eps;
+  // TEMPO_GEMM_LN with ln_stats: the rows' statistics come as partials from the kernel that wrote x (below) instead
+  // of being computed from the A stages.
+  const float2* ln_stats;
+  // row_stats: the output rows' statistics partials, (mean, M2) of each 16-column chunk of the BF16-rounded outputs,
+  // row_stats[row * n / 16 + chunk]: what a folded LayerNorm after this projection needs.
+  float2* row_stats;
   KvStore kv;  // QKV projection: key and value columns also stored into the caches
 };
 
@@ -168,34 +174,101 @@ __device__ __forceinline__ void epilogue_chunk(const RowMajorParams& p, const ui
         if (n0 + j < p.n) v[j] += bf16_to_float(rrow[n0 + j]);
     }
   }
-  if (kStaged) {
-    uint4* cache4 = full_chunk ? reinterpret_cast<uint4*>(kv_destination(p.kv, row, n0)) : nullptr;
+  if (kStaged || full_chunk) {
+    uint4 pk[kCW / 8];
 #pragma unroll
     for (uint32_t q = 0; q < kCW / 8; ++q) {
-      uint4 w;
-      w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-      w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-      w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-      w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-      reinterpret_cast<uint4*>(stage_row)[q ^ swizzle] = w;
-      if (cache4 != nullptr) cache4[q] = w;
+      pk[q].x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+      pk[q].y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+      pk[q].z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+      pk[q].w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
     }
-  } else if (full_chunk) {
+    uint4* cache4 = full_chunk ? reinterpret_cast<uint4*>(kv_destination(p.kv, row, n0)) : nullptr;
     uint4* o4 = reinterpret_cast<uint4*>(orow + n0);
-    uint4* cache4 = reinterpret_cast<uint4*>(kv_destination(p.kv, row, n0));
 #pragma unroll
     for (uint32_t q = 0; q < kCW / 8; ++q) {
-      uint4 w;
-      w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
-      w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
-      w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
-      w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
-      o4[q] = w;
-      if (cache4 != nullptr) cache4[q] = w;
+      if (kStaged) {
+        reinterpret_cast<uint4*>(stage_row)[q ^ swizzle] = pk[q];
+      } else {
+        o4[q] = pk[q];
+      }
+      if (cache4 != nullptr) cache4[q] = pk[q];
+    }
+    // The statistics of each whole 16-column chunk of what was stored (the host guarantees N % 16 == 0).
+    if (p.row_stats != nullptr) {
+#pragma unroll
+      for (uint32_t c = 0; c < kCW / 16; ++c) {
+        if (n0 + 16 * (c + 1) > p.n) break;
+        float lo[8], hi[8], w[16];
+        unpack8(pk[2 * c], lo);
+        unpack8(pk[2 * c + 1], hi);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          w[j] = lo[j];
+          w[8 + j] = hi[j];
+        }
+        p.row_stats[size_t(row) * (p.n / 16) + n0 / 16 + c] = chunk_stats16(w);
+      }
     }
   } else {
     for (uint32_t j = 0; j < kCW; ++j)
       if (n0 + j < p.n) orow[n0 + j] = float_to_bf16(v[j]);
+    // A 32-column chunk whose second half lies past N: the first half's statistics.
+    if (p.row_stats != nullptr && kCW == 32 && n0 + 16 <= p.n) {
+      float w[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) w[j] = bf16_to_float(float_to_bf16(v[j]));
+      p.row_stats[size_t(row) * (p.n / 16) + n0 / 16] = chunk_stats16(w);
+    }
+  }
+}
+
+// The mean and 1 / sqrt(variance + eps) of rows row0 .. row0 + nrows - 1 (nrows <= 8) from their (mean, M2) partials
+// of 16 columns each (`chunks` <= 64 per row, written by the kernel that produced the rows), by one warp: every
+// partial is loaded first (lane l takes chunks l and l + 32 of each row), then per row the mean of the chunk means
+// and M2 = sum M2_c + 16 sum (mean_c - mean)^2, each summed by a fixed shuffle tree, the eight rows' trees side by
+// side. Lane i writes mean_out[i] and rstd_out[i] for row row0 + i. Kept out of line so its registers do not add to
+// the epilogue's.
+__device__ __noinline__ void combine_row_stats_warp(const float2* stats, uint32_t chunks, uint32_t row0,
+                                                    uint32_t nrows, float eps, float* mean_out, float* rstd_out,
+                                                    uint32_t lane) {
+  float2 lo[8], hi[8];
+#pragma unroll
+  for (uint32_t i = 0; i < 8; ++i) {
+    const float2* row = stats + size_t(row0 + i) * chunks;
+    lo[i] = i < nrows && lane < chunks ? __ldcg(row + lane) : make_float2(0.f, 0.f);
+    hi[i] = i < nrows && lane + 32 < chunks ? __ldcg(row + lane + 32) : make_float2(0.f, 0.f);
+  }
+  const float inv_chunks = 1.f / float(chunks);
+  float mean[8], m2[8];
+#pragma unroll
+  for (uint32_t i = 0; i < 8; ++i) mean[i] = lo[i].x + hi[i].x;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) mean[i] += __shfl_xor_sync(0xFFFFFFFFu, mean[i], o);
+#pragma unroll
+  for (uint32_t i = 0; i < 8; ++i) {
+    mean[i] *= inv_chunks;
+    const float dl = lo[i].x - mean[i], dh = hi[i].x - mean[i];
+    m2[i] = (lane < chunks ? fmaf(16.f * dl, dl, lo[i].y) : 0.f) +
+            (lane + 32 < chunks ? fmaf(16.f * dh, dh, hi[i].y) : 0.f);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (uint32_t i = 0; i < 8; ++i) m2[i] += __shfl_xor_sync(0xFFFFFFFFu, m2[i], o);
+  if (lane < nrows) {
+    // lane i keeps row i's values (selects: an array indexed by the lane would go to local memory)
+    float mu = mean[0], sq = m2[0];
+#pragma unroll
+    for (uint32_t i = 1; i < 8; ++i)
+      if (lane == i) {
+        mu = mean[i];
+        sq = m2[i];
+      }
+    mean_out[lane] = mu;
+    rstd_out[lane] = rsqrtf(sq / float(chunks * 16) + eps);
   }
 }
 
@@ -289,9 +362,9 @@ __global__ void __launch_bounds__(kRowThreads, 1)
   constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
 
   if (threadIdx.x == 0) {
-    // With a folded LayerNorm the epilogue warps also read each A stage of the first tile (its rows' statistics):
-    // a stage is free once the MMA and those sixteen warps are done with it.
-    const uint32_t empty_count = LN ? 1u + kRowEpiThreads / 32 : 1u;
+    // With a folded LayerNorm whose statistics are computed here the epilogue warps also read each A stage of the
+    // first tile: a stage is free once the MMA and those sixteen warps are done with it.
+    const uint32_t empty_count = LN && p.ln_stats == nullptr ? 1u + kRowEpiThreads / 32 : 1u;
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], empty_count);
@@ -425,8 +498,18 @@ __global__ void __launch_bounds__(kRowThreads, 1)
       // The first tile's row statistics from its A stages as they stream in for the MMA, ready with the accumulator.
       const uint32_t first_block = blockIdx.x / p.n_tiles;
       const uint32_t rows = p.m - first_block * 128 < 128u ? p.m - first_block * 128 : 128u;
-      const bool ok = ln_stats_from_stages(smem, L::kStageBytes, STAGES, full, empty, kblocks, rows, p.k, p.ln_eps,
-                                           ln_mean, ln_rstd, threadIdx.x - 64, lane, abort_flag);
+      bool ok = true;
+      if (p.ln_stats != nullptr) {
+        // From the partials of the kernel that wrote the rows (it has finished: the wait above): epilogue warp w
+        // takes rows 8 w .. 8 w + 7.
+        const uint32_t r0 = 8 * ((threadIdx.x - 64) / 32);
+        if (r0 < rows)
+          combine_row_stats_warp(p.ln_stats, p.k / 16, first_block * 128 + r0, rows - r0 < 8 ? rows - r0 : 8u,
+                                 p.ln_eps, ln_mean + r0, ln_rstd + r0, lane);
+      } else {
+        ok = ln_stats_from_stages(smem, L::kStageBytes, STAGES, full, empty, kblocks, rows, p.k, p.ln_eps, ln_mean,
+                                  ln_rstd, threadIdx.x - 64, lane, abort_flag);
+      }
       ln_block = first_block;
       if (!ok || !epi_sync()) ln_block = 0xFFFFFFFFu;  // (a timeout: the tile loop below gives up as well)
     }
@@ -754,8 +837,11 @@ struct SplitSmem {
   static constexpr uint32_t kStagingBytes = (kEpilogueThreads / 32) * 32 * kHalfCols * 4;
   static_assert(kStagingBytes <= 2 * kStageBytes, "split-K staging exceeds two ring stages");
   static constexpr uint32_t kBarriers = 2 * STAGES + 3;  // full, empty, acc_full, final, red_full
+  // A folded LayerNorm's mean and rstd of the owned rows, then the tile's column sums and folded bias.
+  static constexpr uint32_t kLnBytes = (2 * kRowsPer + 2 * BN) * 4;
   __host__ __device__ static constexpr uint32_t red_offset(uint32_t stages) { return stages * kStageBytes; }
-  __host__ __device__ static constexpr uint32_t barrier_offset(uint32_t stages) { return red_offset(stages) + kRedBytes; }
+  __host__ __device__ static constexpr uint32_t ln_offset(uint32_t stages) { return red_offset(stages) + kRedBytes; }
+  __host__ __device__ static constexpr uint32_t barrier_offset(uint32_t stages) { return ln_offset(stages) + kLnBytes; }
   __host__ __device__ static constexpr uint32_t bytes(uint32_t stages) {
     return barrier_offset(stages) + kBarriers * 8 + 16 + 1024;
   }
@@ -776,11 +862,6 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t local_smem_addr, uint32
   uint32_t remote;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_smem_addr), "r"(rank));
   return remote;
-}
-
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
-               : "memory");
 }
 
 // A bulk copy from this CTA's shared memory into another CTA's of the cluster (both addresses 16-byte aligned, the
@@ -814,6 +895,10 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t stages = p.stages;
   float* red = reinterpret_cast<float*>(smem + L::red_offset(stages));
+  float* ln_mu = reinterpret_cast<float*>(smem + L::ln_offset(stages));
+  float* ln_rs = ln_mu + L::kRowsPer;
+  float* ln_cs = ln_rs + L::kRowsPer;
+  float* ln_b = ln_cs + BN;
   float* staging = reinterpret_cast<float*>(smem);  // the operand ring, idle once the accumulator is final
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::barrier_offset(stages));
   uint64_t* full = bars;
@@ -942,6 +1027,21 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
                        ? *reinterpret_cast<const uint4*>(p.residual + size_t(row) * p.ldr + col)
                        : make_uint4(0, 0, 0, 0);
     }
+    // A folded LayerNorm: the owned rows' mean and rstd from the partials of the kernel that wrote the rows (epilogue
+    // warp w takes kRowsPer / 8 of them), and the tile's column sums and folded bias, in shared memory before phase 2.
+    const bool ln = p.ln_stats != nullptr;
+    if (ln) {
+      constexpr uint32_t kPerWarp = L::kRowsPer / 8;
+      const uint32_t r0 = (t / 32) * kPerWarp, row0 = m_blk * 128 + rank * L::kRowsPer + r0;
+      const uint32_t nrows = row0 >= p.m ? 0u : (p.m - row0 < kPerWarp ? p.m - row0 : kPerWarp);
+      if (nrows > 0)
+        combine_row_stats_warp(p.ln_stats, p.k / 16, row0, nrows, p.ln_eps, ln_mu + r0, ln_rs + r0, lane);
+      if (t < uint32_t(BN)) {
+        const uint32_t col = n_blk * BN + t;
+        ln_cs[t] = col < p.n ? __ldg(p.ln_colsum + col) : 0.f;
+        ln_b[t] = col < p.n ? __ldg(p.ln_bias + col) : 0.f;
+      }
+    }
 
     // Phase 1: warp (quarter q, half h) holds tile rows 32q .. 32q + 31 x columns h * BN / 2 ...; each lane's
     // half-row goes to its owner's block [rank][h], directly if this CTA owns it, else through the warp's staging
@@ -983,7 +1083,9 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     const bool have_all = have_acc && mbar_wait(red_full, 0, kWatchOther, abort_flag);
 
     if (have_all && !*abort_flag) {
-      // Phase 2: sum the owned rows' partials in rank order, then bias / GELU / residual and 16-byte BF16 stores.
+      // Phase 2: sum the owned rows' partials in rank order, then the folded LayerNorm, bias / GELU / residual and
+      // 16-byte BF16 stores (and the stored rows' statistics). A warp leaves the loop only as a whole (the item bound
+      // is a multiple of 32), so the two lanes of a 16-column chunk always meet at the shuffle.
 #pragma unroll
       for (uint32_t i = 0; i < kItems; ++i) {
         const uint32_t item = t + i * kEpilogueThreads;
@@ -991,7 +1093,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         const uint32_t lr = item / kChunks, c8 = item % kChunks;
         const uint32_t row = m_blk * 128 + rank * L::kRowsPer + lr;
         const uint32_t col = n_blk * BN + c8 * 8;
-        if (row >= p.m || col >= p.n) continue;
+        const bool valid = row < p.m && col < p.n;
         const uint32_t h = c8 / (kChunks / 2), cc = c8 % (kChunks / 2);
         float v[8];
 #pragma unroll
@@ -1002,6 +1104,11 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           const float4 x = row_base[(2 * cc) ^ (lr & 7u)], y = row_base[(2 * cc + 1) ^ (lr & 7u)];
           v[0] += x.x; v[1] += x.y; v[2] += x.z; v[3] += x.w;
           v[4] += y.x; v[5] += y.y; v[6] += y.z; v[7] += y.w;
+        }
+        if (ln) {
+          const float mu = ln_mu[lr], rs = ln_rs[lr];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] = fmaf(rs, fmaf(-mu, ln_cs[c8 * 8 + j], v[j]), ln_b[c8 * 8 + j]);
         }
         if (p.bias != nullptr) {
           const uint32_t ws[4] = {pre_bias[i].x, pre_bias[i].y, pre_bias[i].z, pre_bias[i].w};
@@ -1033,6 +1140,25 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         o.y = pack_bf16x2(v[2], v[3]);
         o.z = pack_bf16x2(v[4], v[5]);
         o.w = pack_bf16x2(v[6], v[7]);
+        if (p.row_stats != nullptr) {
+          // Lanes 2j and 2j + 1 hold the two 8-column halves of one 16-column chunk of the row.
+          float w[8];
+          unpack8(o, w);
+          float sum = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) sum += w[j];
+          sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+          const float mean = sum * (1.f / 16.f);
+          float m2 = 0.f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float d = w[j] - mean;
+            m2 = fmaf(d, d, m2);
+          }
+          m2 += __shfl_xor_sync(0xFFFFFFFFu, m2, 1);
+          if (valid && (c8 & 1u) == 0) p.row_stats[size_t(row) * (p.n / 16) + col / 16] = make_float2(mean, m2);
+        }
+        if (!valid) continue;
         *reinterpret_cast<uint4*>(p.out + size_t(row) * p.ldo + col) = o;
         uint4* cache4 = reinterpret_cast<uint4*>(kv_destination(p.kv, row, col));
         if (cache4 != nullptr) *cache4 = o;
@@ -1424,12 +1550,13 @@ struct LnFold {
   const float* colsum = nullptr;
   const float* bias = nullptr;
   float eps = 0.f;
+  const float2* stats = nullptr;  // the rows' statistics partials from their producer (else computed in-kernel)
 };
 
 static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
                               const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m, uint32_t n,
                               uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx, const KvStore& kv,
-                              const LnFold& ln, void* stream);
+                              const LnFold& ln, void* stream, float2* row_stats = nullptr);
 
 extern "C" tempo_status tempo_gemm(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
                                    const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m,
@@ -1457,11 +1584,52 @@ extern "C" tempo_status tempo_gemm_qkv(const void* a, uint32_t lda, const void* 
                    stream);
 }
 
+extern "C" tempo_status tempo_gemm_rowstats(const void* a, uint32_t lda, const void* w_t, uint32_t ldw,
+                                            const void* bias, const void* residual, uint32_t ldr, void* out,
+                                            uint32_t ldo, uint32_t m, uint32_t n, uint32_t k, uint32_t flags,
+                                            float* row_stats, void* stream) {
+  if (row_stats == nullptr || (reinterpret_cast<uintptr_t>(row_stats) & 7u) || n % 16 ||
+      (flags & (TEMPO_GEMM_LN | TEMPO_GEMM_ARGMAX)))
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm_rowstats: 8-byte aligned statistics, N (%u) a multiple of 16, no argmax "
+                "or folded LayerNorm", n);
+  return gemm_impl(a, lda, w_t, ldw, bias, residual, ldr, out, ldo, m, n, k, flags, nullptr, nullptr, KvStore{},
+                   LnFold{}, stream, reinterpret_cast<float2*>(row_stats));
+}
+
+static tempo_status gemm_ln_impl(const void* x, uint32_t ldx, const void* w_t_folded, uint32_t ldw,
+                                 const float* colsum, const float* bias_folded, float epsilon, const float2* stats,
+                                 void* out, uint32_t ldo, uint32_t m, uint32_t n, uint32_t k, uint32_t flags,
+                                 void* k_cache, void* v_cache, uint32_t seqs, uint32_t heads, uint32_t head,
+                                 uint32_t capacity, const int32_t* positions, void* stream);
+
 extern "C" tempo_status tempo_gemm_ln(const void* x, uint32_t ldx, const void* w_t_folded, uint32_t ldw,
                                       const float* colsum, const float* bias_folded, float epsilon, void* out,
                                       uint32_t ldo, uint32_t m, uint32_t n, uint32_t k, uint32_t flags, void* k_cache,
                                       void* v_cache, uint32_t seqs, uint32_t heads, uint32_t head, uint32_t capacity,
                                       const int32_t* positions, void* stream) {
+  return gemm_ln_impl(x, ldx, w_t_folded, ldw, colsum, bias_folded, epsilon, nullptr, out, ldo, m, n, k, flags,
+                      k_cache, v_cache, seqs, heads, head, capacity, positions, stream);
+}
+
+extern "C" tempo_status tempo_gemm_ln_rowstats(const void* x, uint32_t ldx, const void* w_t_folded, uint32_t ldw,
+                                               const float* colsum, const float* bias_folded, float epsilon,
+                                               const float* row_stats, void* out, uint32_t ldo, uint32_t m, uint32_t n,
+                                               uint32_t k, uint32_t flags, void* k_cache, void* v_cache, uint32_t seqs,
+                                               uint32_t heads, uint32_t head, uint32_t capacity,
+                                               const int32_t* positions, void* stream) {
+  if (row_stats == nullptr || (reinterpret_cast<uintptr_t>(row_stats) & 7u) || k % 16 || k > 1024)
+    return fail(TEMPO_ERR_VALUE, "tempo_gemm_ln_rowstats: 8-byte aligned statistics, K (%u) a multiple of 16, <= 1024",
+                k);
+  return gemm_ln_impl(x, ldx, w_t_folded, ldw, colsum, bias_folded, epsilon,
+                      reinterpret_cast<const float2*>(row_stats), out, ldo, m, n, k, flags, k_cache, v_cache, seqs,
+                      heads, head, capacity, positions, stream);
+}
+
+static tempo_status gemm_ln_impl(const void* x, uint32_t ldx, const void* w_t_folded, uint32_t ldw,
+                                 const float* colsum, const float* bias_folded, float epsilon, const float2* stats,
+                                 void* out, uint32_t ldo, uint32_t m, uint32_t n, uint32_t k, uint32_t flags,
+                                 void* k_cache, void* v_cache, uint32_t seqs, uint32_t heads, uint32_t head,
+                                 uint32_t capacity, const int32_t* positions, void* stream) {
   if (colsum == nullptr || bias_folded == nullptr || !aligned16(colsum) || !aligned16(bias_folded))
     return fail(TEMPO_ERR_VALUE, "tempo_gemm_ln: column sums and folded bias are needed, 16-byte aligned");
   if (flags & ~TEMPO_GEMM_GELU) return fail(TEMPO_ERR_VALUE, "tempo_gemm_ln: only TEMPO_GEMM_GELU may be set");
@@ -1477,7 +1645,7 @@ extern "C" tempo_status tempo_gemm_ln(const void* x, uint32_t ldx, const void* w
                  capacity, width};
   }
   return gemm_impl(x, ldx, w_t_folded, ldw, nullptr, nullptr, 0, out, ldo, m, n, k, flags | TEMPO_GEMM_LN, nullptr,
-                   nullptr, kv, LnFold{colsum, bias_folded, epsilon}, stream);
+                   nullptr, kv, LnFold{colsum, bias_folded, epsilon, stats}, stream);
 }
 
 extern "C" tempo_status tempo_gemm_norm(const void* x, uint32_t ldx, const void* gamma, const void* beta,
@@ -1521,7 +1689,7 @@ extern "C" tempo_status tempo_gemm_norm(const void* x, uint32_t ldx, const void*
 static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint32_t ldw, const void* bias,
                               const void* residual, uint32_t ldr, void* out, uint32_t ldo, uint32_t m, uint32_t n,
                               uint32_t k, uint32_t flags, float* part_val, int32_t* part_idx, const KvStore& kv,
-                              const LnFold& ln, void* stream) {
+                              const LnFold& ln, void* stream, float2* row_stats) {
   if (m == 0 || n == 0 || k == 0) return fail(TEMPO_ERR_VALUE, "tempo_gemm: empty problem %ux%ux%u", m, n, k);
   if (k % 8 || lda % 8 || ldw % 8 || lda < k || ldw < k)
     return fail(TEMPO_ERR_VALUE, "tempo_gemm: K (%u) and the row strides (%u, %u) must be multiples of 8 and >= K", k,
@@ -1549,6 +1717,7 @@ static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint
   p.ldr = ldr;
   p.flags = flags;
   p.kv = kv;
+  p.row_stats = row_stats;
   const bool ln_mode = (flags & TEMPO_GEMM_LN) != 0;
   if (ln_mode) {
     p.ln_x = static_cast<const uint16_t*>(a);
@@ -1556,15 +1725,39 @@ static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint
     p.ln_colsum = ln.colsum;
     p.ln_bias = ln.bias;
     p.ln_eps = ln.eps;
+    p.ln_stats = ln.stats;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // A handful of rows (decode of a few sequences): stream the weights on the CUDA cores instead.
-  if (m <= 8 && !ln_mode) {
+  // A handful of rows (decode of a few sequences): stream the weights on the CUDA cores instead (no statistics).
+  if (m <= 8 && !ln_mode && row_stats == nullptr) {
     const tempo_status gemv = gemv_dispatch(a, lda, w_t, ldw, bias, residual, ldr, out, ldo, m, n, k, flags, part_val,
                                             part_idx, kv, st);
     if (gemv != TEMPO_ERR_VALUE) return gemv;
   }
   if (argmax) return launch_rowmajor<256, 4>(a, lda, w_t, ldw, p, st);
+  // With the statistics from their producer, the folded LayerNorm runs wherever the plain projection would: narrow
+  // full-K tiles for one 128-row block, else split-K.
+  const bool ln_partials = ln_mode && ln.stats != nullptr;
+  if (ln_partials && m <= 128 && k <= 1024) {
+    const uint32_t sms = uint32_t(sm_count());
+    if ((n + 15) / 16 <= sms) return launch_rowmajor<16, 8, false, true>(a, lda, w_t, ldw, p, st);
+    if ((n + 31) / 32 <= sms) return launch_rowmajor<32, 8, false, true>(a, lda, w_t, ldw, p, st);
+  }
+  uint32_t bn = 0, splits = 0;
+  if (ln_partials && n % 8 == 0 && pick_split(m, n, k, &bn, &splits)) {
+    if (bn == 128) {
+      switch (splits) {
+        case 2: return launch_splitk<128, 2, 4>(a, lda, w_t, ldw, p, st);
+        case 4: return launch_splitk<128, 4, 4>(a, lda, w_t, ldw, p, st);
+        default: return launch_splitk<128, 8, 4>(a, lda, w_t, ldw, p, st);
+      }
+    }
+    switch (splits) {
+      case 2: return launch_splitk<64, 2, 6>(a, lda, w_t, ldw, p, st);
+      case 4: return launch_splitk<64, 4, 6>(a, lda, w_t, ldw, p, st);
+      default: return launch_splitk<64, 8, 6>(a, lda, w_t, ldw, p, st);
+    }
+  }
   if (ln_mode) {
     // The folded LayerNorm takes each tile's row statistics from its own A stages, so every CTA gets one tile: the
     // narrowest tiles (the most CTAs) that need no more tiles than SMs.
@@ -1584,9 +1777,7 @@ static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint
     if ((n + 31) / 32 <= sms) return launch_rowmajor<32, 8>(a, lda, w_t, ldw, p, st);
   }
   // Small M (decode): split the contraction over a cluster so every SM has work.
-  uint32_t bn = 0, splits = 0;
-  // The folded LayerNorm needs every k of a row in one CTA: no split-K.
-  if (!ln_mode && n % 8 == 0 && pick_split(m, n, k, &bn, &splits)) {
+  if (n % 8 == 0 && pick_split(m, n, k, &bn, &splits)) {
     if (bn == 128) {
       switch (splits) {
         case 2: return launch_splitk<128, 2, 4>(a, lda, w_t, ldw, p, st);

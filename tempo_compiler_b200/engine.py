@@ -84,10 +84,12 @@ class Engine:
         capacity: cache positions per sequence (prompt + decode steps).
         device: the CUDA device.
         fold_layernorms: decode folds each block's two LayerNorms into the QKV and FC projections
-            (``ops.gemm_ln``), so a layer runs five kernels instead of seven (needs more than 8 sequences: 8 or fewer
-            rows take the CUDA-core GEMV path, which has no folded form). Default off: measured side by side on a
-            B200, the in-kernel row statistics slow the projections' operand pipeline by more than the two
-            LayerNorm launches cost (512 sequences: 460 ms of decode folded, 453 ms not; 64 sequences: 110 / 106 ms).
+            (``ops.gemm_ln_rowstats``): the out-projection and the second MLP projection also write the statistics
+            partials of the rows they store (``ops.gemm_rowstats``) and the projection after each combines them, so
+            a layer runs five kernels instead of seven. Needs more than 8 sequences (8 or fewer rows take the
+            CUDA-core path, which normalises inside its projections anyway). Default on for more than 8 sequences:
+            measured side by side on a B200, 64 sequences 653,000-655,000 tokens/s folded against 632,000-633,000
+            (decode step 781-795 us against 827-831), 512 sequences within the run-to-run spread.
         decode_groups: the decode step splits the batch into this many groups of sequences, each on its own CUDA
             stream (default 1). The groups are independent, so one group's bandwidth-bound attention may overlap
             another's projections; on a B200 the extra, smaller launches cost more than the overlap gains (512
@@ -134,7 +136,7 @@ class Engine:
         self.wpe = _bf16(shared["wpe"], self.device)
         self.lnf_g = _bf16(shared["ln_f.g"], self.device)
         self.lnf_b = _bf16(shared["ln_f.b"], self.device)
-        self.fold_layernorms = False if fold_layernorms is None else (fold_layernorms and batch > 8)
+        self.fold_layernorms = (batch > 8) if fold_layernorms is None else (fold_layernorms and batch > 8)
         # decode groups of at most 8 sequences normalise inside their projections (tempo_gemm_norm: same bits, two
         # launches fewer per layer and one fewer per step)
         self.fuse_small_norms = True if fuse_small_norms is None else fuse_small_norms
@@ -164,6 +166,10 @@ class Engine:
         self.dqkv = torch.empty((batch, 3 * width), **bf)
         self.dattn = torch.empty((batch, width), **bf)
         self.dh = torch.empty((batch, shape.ffn), **bf)
+        # the folded LayerNorms' row statistics partials (mean, M2 of each 16 columns), before attention and before
+        # the MLP
+        self.dstats1 = torch.empty((batch, width // 16, 2), dtype=torch.float32, device=self.device)
+        self.dstats2 = torch.empty((batch, width // 16, 2), dtype=torch.float32, device=self.device)
         self.ids = torch.zeros(batch, **i32)
         self.positions = torch.zeros(batch, **i32)
         self.seq_index = torch.arange(batch, **i32)
@@ -227,16 +233,19 @@ class Engine:
         ops.gemm(h, lw.w_out, bias=lw.b_out, residual=x, out=x)
 
     def _folded_decode_layer(self, lw: LayerWeights, index: int, x, qkv, attn, h, seqs: slice) -> None:
-        """One decode block with both LayerNorms folded into the projections after them."""
+        """One decode block with both LayerNorms folded into the projections after them: each residual projection
+        also writes the statistics partials of the rows it stores, and the next projection combines them."""
         k_cache, v_cache = self.k_cache[index][seqs], self.v_cache[index][seqs]
         positions = self.positions[seqs]
+        stats1, stats2 = self.dstats1[seqs], self.dstats2[seqs]
         w, cs, bf = lw.qkv_folded
-        ops.gemm_ln(x, w, cs, bf, epsilon=LN_EPSILON, out=qkv, k_cache=k_cache, v_cache=v_cache, positions=positions)
+        ops.gemm_ln_rowstats(x, w, cs, bf, stats1, epsilon=LN_EPSILON, out=qkv, k_cache=k_cache, v_cache=v_cache,
+                             positions=positions)
         ops.decode_attention(qkv, k_cache, v_cache, positions, length_offset=1, out=attn)
-        ops.gemm(attn, lw.w_proj, bias=lw.b_proj, residual=x, out=x)
+        ops.gemm_rowstats(attn, lw.w_proj, stats2, bias=lw.b_proj, residual=x, out=x)
         w, cs, bf = lw.fc_folded
-        ops.gemm_ln(x, w, cs, bf, epsilon=LN_EPSILON, gelu=True, out=h)
-        ops.gemm(h, lw.w_out, bias=lw.b_out, residual=x, out=x)
+        ops.gemm_ln_rowstats(x, w, cs, bf, stats2, epsilon=LN_EPSILON, gelu=True, out=h)
+        ops.gemm_rowstats(h, lw.w_out, stats1, bias=lw.b_out, residual=x, out=x)
 
     def prefill(self, token_ids: torch.Tensor) -> None:
         """Runs the prompts ([batch, prompt] int32 on the device) through every layer, filling the caches, and writes
@@ -288,6 +297,8 @@ class Engine:
             return
         dx, dln, dqkv, dattn, dh = (t[seqs] for t in (self.dx, self.dln, self.dqkv, self.dattn, self.dh))
         ops.embed(self.ids[seqs], self.positions[seqs], self.wte, self.wpe, out=dx)
+        if self.fold_layernorms:
+            ops.row_stats(dx, self.dstats1[seqs])
         for index, lw in enumerate(self.layers):
             self._layer(lw, index, dx, dln, dqkv, dattn, dh, decode=True, seqs=seqs)
         # the token decoded at position p is generated token p - prompt + 1

@@ -84,6 +84,10 @@ _SIGNATURES = {
                        _vp],
     "tempo_gemm_ln": [_vp, _u32, _vp, _u32, _vp, _vp, _f32, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp, _u32, _u32,
                       _u32, _u32, _vp, _vp],
+    "tempo_gemm_rowstats": [_vp, _u32, _vp, _u32, _vp, _vp, _u32, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp],
+    "tempo_gemm_ln_rowstats": [_vp, _u32, _vp, _u32, _vp, _vp, _f32, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _vp,
+                               _u32, _u32, _u32, _u32, _vp, _vp],
+    "tempo_row_stats": [_vp, _u32, _u32, _u32, _vp, _vp],
     "tempo_layernorm": [_vp, _u32, _vp, _vp, _vp, _u32, _u32, _f32, _vp],
     "tempo_embed": [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _vp],
     "tempo_attention_prefill": [_vp, _vp, _u32, _u32, _u32, _u32, _vp],

@@ -113,6 +113,69 @@ def gemm_ln(x: torch.Tensor, w_folded: torch.Tensor, colsum: torch.Tensor, bias_
     return out
 
 
+def gemm_rowstats(a: torch.Tensor, w_t: torch.Tensor, row_stats: torch.Tensor, *, bias: torch.Tensor | None = None,
+                  residual: torch.Tensor | None = None, gelu: bool = False,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """gemm that also writes the statistics partials of its BF16 output rows into row_stats [M, N / 16, 2] (FP32
+    mean and M2 of each 16-column chunk), for the folded LayerNorm of the projection that reads those rows next."""
+    _check(a, torch.bfloat16, "a")
+    _check(w_t, torch.bfloat16, "w_t")
+    _check(row_stats, torch.float32, "row_stats")
+    m, k = a.shape
+    n = w_t.shape[0]
+    if w_t.shape[1] != k:
+        raise ValueError(f"inner dimensions differ: a {tuple(a.shape)}, w_t {tuple(w_t.shape)}")
+    if row_stats.numel() < m * n // 8:
+        raise ValueError(f"row_stats holds {row_stats.numel()} floats, {m * n // 8} needed")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=a.device)
+    _check(out, torch.bfloat16, "out")
+    _launch("tempo_gemm_rowstats", a.data_ptr(), k, w_t.data_ptr(), k, _ptr(bias), _ptr(residual), n, out.data_ptr(),
+            n, m, n, k, _lib.GEMM_GELU if gelu else 0, row_stats.data_ptr(), _stream())
+    return out
+
+
+def gemm_ln_rowstats(x: torch.Tensor, w_folded: torch.Tensor, colsum: torch.Tensor, bias_folded: torch.Tensor,
+                     row_stats: torch.Tensor, *, epsilon: float = 1e-5, gelu: bool = False,
+                     out: torch.Tensor | None = None, k_cache: torch.Tensor | None = None,
+                     v_cache: torch.Tensor | None = None, positions: torch.Tensor | None = None) -> torch.Tensor:
+    """gemm_ln with the rows' statistics combined from row_stats [M, K / 16, 2] (gemm_rowstats' or row_stats'
+    partials of x) instead of computed in the kernel."""
+    _check(x, torch.bfloat16, "x")
+    _check(w_folded, torch.bfloat16, "w_folded")
+    _check(colsum, torch.float32, "colsum")
+    _check(bias_folded, torch.float32, "bias_folded")
+    _check(row_stats, torch.float32, "row_stats")
+    m, k = x.shape
+    n = w_folded.shape[0]
+    if w_folded.shape[1] != k:
+        raise ValueError(f"inner dimensions differ: x {tuple(x.shape)}, w_folded {tuple(w_folded.shape)}")
+    if row_stats.numel() < m * k // 8:
+        raise ValueError(f"row_stats holds {row_stats.numel()} floats, {m * k // 8} needed")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+    _check(out, torch.bfloat16, "out")
+    seqs = heads = head = capacity = 0
+    if k_cache is not None:
+        seqs, heads, capacity, head = k_cache.shape
+    _launch("tempo_gemm_ln_rowstats", x.data_ptr(), k, w_folded.data_ptr(), k, colsum.data_ptr(),
+            bias_folded.data_ptr(), float(epsilon), row_stats.data_ptr(), out.data_ptr(), out.shape[1], m, n, k,
+            _lib.GEMM_GELU if gelu else 0, _ptr(k_cache), _ptr(v_cache), seqs, heads, head, capacity,
+            _ptr(positions), _stream())
+    return out
+
+
+def row_stats(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """The statistics partials of x's rows ([M, K / 16, 2] FP32 into `out`), as gemm_rowstats writes them."""
+    _check(x, torch.bfloat16, "x")
+    _check(out, torch.float32, "out")
+    m, k = x.shape
+    if out.numel() < m * k // 8:
+        raise ValueError(f"out holds {out.numel()} floats, {m * k // 8} needed")
+    _launch("tempo_row_stats", x.data_ptr(), x.stride(0), m, k, out.data_ptr(), _stream())
+    return out
+
+
 def gemm_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, w_t: torch.Tensor, *, epsilon: float = 1e-5,
               bias: torch.Tensor | None = None, gelu: bool = False, out: torch.Tensor | None = None,
               k_cache: torch.Tensor | None = None, v_cache: torch.Tensor | None = None,

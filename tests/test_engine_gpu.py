@@ -81,8 +81,9 @@ def test_folded_layernorm_decode_matches_the_oracle() -> None:
     tokens = engine.generate(ids, steps)
     for s in range(0, batch, 3):
         _check_teacher_forced(layers, shared, ids[s], tokens[s])
-    unfolded = Engine(layers, shared, batch=batch, prompt=prompt, capacity=prompt + steps)
+    unfolded = Engine(layers, shared, batch=batch, prompt=prompt, capacity=prompt + steps, fold_layernorms=False)
     assert not unfolded.fold_layernorms
+    assert Engine(layers, shared, batch=batch, prompt=prompt, capacity=prompt + steps).fold_layernorms  # the default
     plain = unfolded.generate(ids, steps)
     # the two decodes may part only at a near-tie; most sequences agree throughout
     assert (plain == tokens).all(axis=1).sum() >= batch - 2
