@@ -42,8 +42,8 @@ __device__ __forceinline__ uint32_t decode_cluster_rank() {
   return r;
 }
 
-// KI keys per lane group per iteration (a warp covers 4 KI keys): 8 keeps 16 loads per lane in flight for grids of
-// many waves; 4 halves the registers (about 64) so a grid of up to eight CTAs per SM is resident at once.
+// KI keys per lane group per iteration (a warp covers 4 KI keys): 8 keeps 16 loads per lane in flight; 4 halves the
+// registers (71) so up to seven CTAs per SM are resident at once. The host picks between them by grid size.
 template <int KI>
 __global__ void __launch_bounds__(128) decode_attention_kernel(const uint16_t* __restrict__ qkv,
                                                                const uint16_t* __restrict__ k_cache,
@@ -199,12 +199,18 @@ extern "C" tempo_status tempo_decode_attention(const void* qkv, const void* k_ca
   const uint64_t pairs = uint64_t(seqs) * heads, target = uint64_t(sm_count());
   uint32_t chunks = 1;
   while (chunks < kDecodeMaxChunks && pairs * chunks < target && capacity >= 2 * 64 * chunks) chunks *= 2;
-  // A grid that fits at eight CTAs per SM runs the 4-key variant, entirely resident; larger grids the 8-key one.
+  // The bytes each SM keeps in flight bound this kernel until the grid is several waves deep: the 8-key variant has
+  // 32 KB in flight per CTA at 4 CTAs per SM (126 registers), the 4-key one 16 KB at 7 (71 registers). Measured on a
+  // B200 (1088 cached keys, 12 heads): the 8-key variant is faster up to 4 CTAs per SM (13-48 sequences: 12.6-24.7 us
+  // against 16.4-30.8) and again from about 7 per SM, where the 4-key grid no longer fits one wave (88-112 sequences:
+  // 44-60 us against 61-66); the 4-key one between (52-72 sequences: 31.2-37.7 us against 33.3-39.3). Fewer pairs than
+  // SMs (a handful of sequences, split over clusters or not) keep the 4-key variant: the persistent decode step of up
+  // to 8 sequences computes their stretches with its arithmetic, bit for bit.
   const uint64_t ctas = pairs * chunks;
-  const bool small = single_wave(ctas, 8) != 0;
-  auto kernel = small ? decode_attention_kernel<4> : decode_attention_kernel<8>;
+  const bool four = pairs < target || (ctas > 4 * target && ctas <= 6 * target);
+  auto kernel = four ? decode_attention_kernel<4> : decode_attention_kernel<8>;
   return launch(kernel, dim3(chunks, heads, seqs), dim3(128), 0, static_cast<cudaStream_t>(stream), chunks,
                 "decode_attention_kernel", static_cast<const uint16_t*>(qkv), static_cast<const uint16_t*>(k_cache),
                 static_cast<const uint16_t*>(v_cache), lengths, length_offset, static_cast<uint16_t*>(out), heads,
-                capacity, small ? 1u : single_wave(ctas, 4));
+                capacity, single_wave(ctas, four ? 7 : 4));
 }
