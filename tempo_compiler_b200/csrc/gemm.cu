@@ -18,6 +18,10 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "common.cuh"
 #include "host.hpp"
 
@@ -1518,6 +1522,74 @@ tempo_status launch_pair(const void* a, uint32_t lda, const void* w_t, uint32_t 
 // two or more splits) that still fit one wave, each split keeping at least two k-blocks. Returns false when the
 // plain kernel is better (including when only an unsplit grid fits: the persistent kernel runs that without a
 // reduction step).
+// How many clusters of the split-K kernel <BN, SPLITS> the device holds at once (cudaOccupancyMaxActiveClusters at
+// its largest shared-memory size), cached per device; 0 if the query fails. A cluster needs its CTAs' SMs inside one
+// GPC, so a grid of clusters can need a second wave although its CTAs number fewer than the SMs: measured on a B200,
+// 36 clusters of 4 (the QKV projection of 192-256 rows) took 11.4 us against 5.0-5.5 for one wave of full-K tiles.
+template <int BN, int SPLITS, int STAGES>
+uint32_t splitk_resident_clusters() {
+  using L = SplitSmem<BN, SPLITS, STAGES>;
+  static std::mutex mu;
+  static std::map<int, uint32_t> known;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto it = known.find(device);
+  if (it != known.end()) return it->second;
+  auto kernel = gemm_splitk_kernel<BN, SPLITS, STAGES>;
+  uint32_t result = 0;
+  if (set_smem(reinterpret_cast<const void*>(kernel), L::bytes(STAGES)) == TEMPO_OK) {
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(SPLITS);
+    config.blockDim = dim3(kSplitThreads);
+    config.dynamicSmemBytes = L::bytes(STAGES);
+    cudaLaunchAttribute attribute;
+    attribute.id = cudaLaunchAttributeClusterDimension;
+    attribute.val.clusterDim.x = SPLITS;
+    attribute.val.clusterDim.y = 1;
+    attribute.val.clusterDim.z = 1;
+    config.attrs = &attribute;
+    config.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &config) == cudaSuccess && clusters > 0)
+      result = uint32_t(clusters);
+    else
+      (void)cudaGetLastError();
+  }
+  known[device] = result;
+  return result;
+}
+
+uint32_t splitk_resident_clusters(uint32_t bn, uint32_t splits) {
+  if (bn == 128) return splits == 2 ? splitk_resident_clusters<128, 2, 4>()
+                        : splits == 4 ? splitk_resident_clusters<128, 4, 4>() : splitk_resident_clusters<128, 8, 4>();
+  return splits == 2 ? splitk_resident_clusters<64, 2, 6>()
+         : splits == 4 ? splitk_resident_clusters<64, 4, 6>() : splitk_resident_clusters<64, 8, 6>();
+}
+
+// Full-K row-major tiles for a decode-sized product (one wave of tiles covers it): the tile width (16, 32, 64 or
+// 128 columns) that minimises an estimate of the operand time, the slowest CTA's A rows and BN weight rows over K at
+// the rate one SM draws from L2 (about 60 GB/s) plus the whole grid's bytes at the aggregate rate (about 20 TB/s).
+// The constants are fitted to a sweep of the GPT-2 decode projections (64-512 rows, K = 768) on a B200, where the
+// estimate picks a width within 3 % of the fastest in 17 of 18 cases. 0 when no width fits one wave.
+uint32_t pick_full_k_width(uint32_t m, uint32_t n, uint32_t k) {
+  const uint64_t sms = uint64_t(sm_count()), m_tiles = (m + 127) / 128;
+  const double a_rows = m <= 64 ? 64.0 : 128.0;
+  uint32_t best = 0;
+  double best_cost = 0.0;
+  for (uint32_t bn : {16u, 32u, 64u, 128u}) {
+    const uint64_t tiles = m_tiles * ((n + bn - 1) / bn);
+    if (tiles > sms) continue;
+    const double per_cta = (a_rows + bn) * k * 2.0;                // bytes
+    const double cost = per_cta / 60e3 + double(tiles) * per_cta / 20e6;  // microseconds
+    if (best == 0 || cost < best_cost) {
+      best = bn;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
 bool pick_split(uint32_t m, uint32_t n, uint32_t k, uint32_t* bn, uint32_t* splits) {
   const uint32_t sms = uint32_t(sm_count());
   const uint32_t m_tiles = (m + 127) / 128, kblocks = (k + kBK - 1) / kBK;
@@ -1528,6 +1600,7 @@ bool pick_split(uint32_t m, uint32_t n, uint32_t k, uint32_t* bn, uint32_t* spli
     for (uint32_t s : {2u, 4u, 8u}) {
       const uint64_t ctas = uint64_t(tiles) * s;
       if (ctas > sms || kblocks < 2 * s) continue;
+      if (tiles > splitk_resident_clusters(cand_bn, s)) continue;  // the clusters must all be resident at once
       if (ctas > best_ctas) {
         best_ctas = uint32_t(ctas);
         *bn = cand_bn;
@@ -1738,10 +1811,14 @@ static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint
   // With the statistics from their producer, the folded LayerNorm runs wherever the plain projection would: narrow
   // full-K tiles for one 128-row block, else split-K.
   const bool ln_partials = ln_mode && ln.stats != nullptr;
-  if (ln_partials && m <= 128 && k <= 1024) {
-    const uint32_t sms = uint32_t(sm_count());
-    if ((n + 15) / 16 <= sms) return launch_rowmajor<16, 8, false, true>(a, lda, w_t, ldw, p, st);
-    if ((n + 31) / 32 <= sms) return launch_rowmajor<32, 8, false, true>(a, lda, w_t, ldw, p, st);
+  if (ln_partials && k <= 1024) {
+    switch (pick_full_k_width(m, n, k)) {
+      case 16: return launch_rowmajor<16, 8, false, true>(a, lda, w_t, ldw, p, st);
+      case 32: return launch_rowmajor<32, 8, false, true>(a, lda, w_t, ldw, p, st);
+      case 64: return launch_rowmajor<64, 8, false, true>(a, lda, w_t, ldw, p, st);
+      case 128: return launch_rowmajor<128, 5, true, true>(a, lda, w_t, ldw, p, st);
+      default: break;
+    }
   }
   uint32_t bn = 0, splits = 0;
   if (ln_partials && n % 8 == 0 && pick_split(m, n, k, &bn, &splits)) {
@@ -1769,12 +1846,16 @@ static tempo_status gemm_impl(const void* a, uint32_t lda, const void* w_t, uint
     if (m_tiles * ((n + 255) / 256) <= sms) return launch_rowmajor<256, 3, true, true>(a, lda, w_t, ldw, p, st);
     return fail(TEMPO_ERR_VALUE, "tempo_gemm_ln: %u x %u needs more than one 128-row tile per SM", m, n);
   }
-  // One 128-row block with a short contraction (the decode projections of up to 128 sequences): narrow tiles over the
-  // whole of K, at most one per SM, need no cross-CTA reduction.
-  if (m <= 128 && k <= 1024) {
-    const uint32_t sms = uint32_t(sm_count());
-    if ((n + 15) / 16 <= sms) return launch_rowmajor<16, 8>(a, lda, w_t, ldw, p, st);
-    if ((n + 31) / 32 <= sms) return launch_rowmajor<32, 8>(a, lda, w_t, ldw, p, st);
+  // A decode-sized product with a short contraction (the decode projections): full-K tiles, at most one per SM, no
+  // cross-CTA reduction; measured faster than split-K at K = 768 from 64 to 512 rows, or level with it.
+  if (k <= 1024 && uint64_t((m + 127) / 128) * ((n + 127) / 128) < uint64_t(sm_count())) {
+    switch (pick_full_k_width(m, n, k)) {
+      case 16: return launch_rowmajor<16, 8>(a, lda, w_t, ldw, p, st);
+      case 32: return launch_rowmajor<32, 8>(a, lda, w_t, ldw, p, st);
+      case 64: return launch_rowmajor<64, 8>(a, lda, w_t, ldw, p, st);
+      case 128: return launch_rowmajor<128, 5, true>(a, lda, w_t, ldw, p, st);
+      default: break;
+    }
   }
   // Small M (decode): split the contraction over a cluster so every SM has work.
   if (n % 8 == 0 && pick_split(m, n, k, &bn, &splits)) {

@@ -158,9 +158,12 @@ def test_block_gemm_deep_contraction_is_exact() -> None:
 
 @pytest.mark.parametrize(("m", "n", "k"), [(128, 256, 64), (1024, 2304, 768), (1000, 768, 768), (512, 3072, 768),
                                            (64, 768, 3072), (300, 200, 136), (4096, 768, 3072), (16000, 768, 768),
-                                           # small-M shapes taking the cluster split-K path (1, 2, 4 and 8 splits)
-                                           (512, 2304, 768), (512, 768, 768), (64, 2304, 768), (33, 768, 3072),
-                                           (200, 3072, 768)])
+                                           # decode-sized shapes: full-K tiles of 16-128 columns at K <= 1024,
+                                           (512, 2304, 768), (512, 768, 768), (64, 2304, 768), (200, 3072, 768),
+                                           (384, 2304, 768), (256, 768, 768),
+                                           # the cluster split-K path beyond (2, 4 and 8 splits)
+                                           (33, 768, 3072), (512, 2304, 2048), (384, 768, 3072), (200, 768, 3072),
+                                           (512, 768, 3072)])
 @pytest.mark.parametrize("epilogue", ["plain", "bias", "gelu", "residual"])
 def test_gemm_matches_fp32_reference(m: int, n: int, k: int, epilogue: str) -> None:
     from tempo_compiler_b200 import ops
