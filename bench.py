@@ -413,7 +413,7 @@ def b200_arm(args) -> int:
 
     # phase split and per-kernel rooflines, timed with CUDA events on the launching stream
     measured, source = peaks()
-    prefill_ms = _time(lambda: engine.prefill(ids_dev), stream, 2)
+    prefill_ms = _time(lambda: engine.prefill(ids_dev, graph=graph), stream, 2)
     decode_ms = _time(lambda: engine.decode(args.decode, graph=graph), stream, 1) if args.decode else 0.0
     roof = _decode_attention_roofline(engine, stream, measured, source)
     gemm_roof = _gemm_roofline(engine, stream, measured, source)

@@ -178,6 +178,7 @@ class Engine:
         self.part_idx = torch.empty((batch, self.tiles), **i32)
         self.tokens: torch.Tensor | None = None
         self._graph: torch.cuda.CUDAGraph | None = None
+        self._prefill_graph: torch.cuda.CUDAGraph | None = None
         self._graph_steps = 0
         groups = 1 if decode_groups is None else decode_groups
         if not 1 <= groups <= batch:
@@ -247,10 +248,31 @@ class Engine:
         ops.gemm_ln_rowstats(x, w, cs, bf, stats2, epsilon=LN_EPSILON, gelu=True, out=h)
         ops.gemm_rowstats(h, lw.w_out, stats1, bias=lw.b_out, residual=x, out=x)
 
-    def prefill(self, token_ids: torch.Tensor) -> None:
+    def prefill(self, token_ids: torch.Tensor, *, graph: bool = False) -> None:
         """Runs the prompts ([batch, prompt] int32 on the device) through every layer, filling the caches, and writes
-        the first generated token of each sequence into ``self.tokens[:, 0]``."""
+        the first generated token of each sequence into ``self.tokens[:, 0]``. With `graph` the layers run as one
+        replay of a CUDA graph captured on first use (the host then issues one launch instead of about a hundred)."""
         self.prompt_ids.copy_(token_ids.reshape(-1))
+        if graph:
+            self._capture_prefill()
+            self._prefill_graph.replay()
+        else:
+            self._prefill_body()
+
+    def _capture_prefill(self) -> None:
+        if self._prefill_graph is not None:
+            return
+        stream = torch.cuda.Stream(device=self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            self._prefill_body()  # warm-up (the replay that follows recomputes the same state from the same prompts)
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self._prefill_body()
+        self._prefill_graph = graph
+
+    def _prefill_body(self) -> None:
         ops.embed(self.prompt_ids, self.prompt_pos, self.wte, self.wpe, out=self.x)
         for index, lw in enumerate(self.layers):
             self._layer(lw, index, self.x, self.ln, self.qkv, self.attn, self.h, decode=False)
@@ -364,7 +386,8 @@ class Engine:
         if self.tokens is None or self.tokens.shape[1] != steps + 1:
             self.tokens = torch.zeros((self.batch, steps + 1), dtype=torch.int32, device=self.device)
             self._graph = None
-        self.prefill(token_ids)
+            self._prefill_graph = None  # both graphs write into the token buffer
+        self.prefill(token_ids, graph=graph)
         self.decode(steps, graph=graph)
         return self.tokens
 
