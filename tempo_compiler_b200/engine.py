@@ -179,6 +179,9 @@ class Engine:
         self.tokens: torch.Tensor | None = None
         self._graph: torch.cuda.CUDAGraph | None = None
         self._prefill_graph: torch.cuda.CUDAGraph | None = None
+        # generate()'s pinned host staging for the prompts and the tokens, kept between calls
+        self._pinned_ids: torch.Tensor | None = None
+        self._pinned_tokens: torch.Tensor | None = None
         self._graph_steps = 0
         groups = 1 if decode_groups is None else decode_groups
         if not 1 <= groups <= batch:
@@ -253,6 +256,10 @@ class Engine:
         the first generated token of each sequence into ``self.tokens[:, 0]``. With `graph` the layers run as one
         replay of a CUDA graph captured on first use (the host then issues one launch instead of about a hundred)."""
         self.prompt_ids.copy_(token_ids.reshape(-1))
+        self._prefill_loaded(graph)
+
+    def _prefill_loaded(self, graph: bool) -> None:
+        """prefill() on the prompts already in ``self.prompt_ids``."""
         if graph:
             self._capture_prefill()
             self._prefill_graph.replay()
@@ -381,22 +388,34 @@ class Engine:
         """Prefill plus `steps` decode steps on device-resident prompts; returns [batch, steps + 1] int32 tokens."""
         if token_ids.shape != (self.batch, self.prompt):
             raise ValueError(f"expected prompts of shape {(self.batch, self.prompt)}, got {tuple(token_ids.shape)}")
+        self.prompt_ids.copy_(token_ids.reshape(-1))
+        return self._run_loaded(steps, graph)
+
+    def _run_loaded(self, steps: int, graph: bool) -> torch.Tensor:
         if self.prompt + steps > self.capacity:
             raise ValueError(f"{self.prompt} prompt tokens + {steps} steps exceed the cache capacity {self.capacity}")
         if self.tokens is None or self.tokens.shape[1] != steps + 1:
             self.tokens = torch.zeros((self.batch, steps + 1), dtype=torch.int32, device=self.device)
             self._graph = None
             self._prefill_graph = None  # both graphs write into the token buffer
-        self.prefill(token_ids, graph=graph)
+        self._prefill_loaded(graph)
         self.decode(steps, graph=graph)
         return self.tokens
 
     def generate(self, token_ids: np.ndarray, steps: int, *, graph: bool = True) -> np.ndarray:
-        """The end-to-end call: host prompts in, host tokens out ([batch, steps + 1])."""
-        host = torch.from_numpy(np.ascontiguousarray(token_ids, dtype=np.int32)).pin_memory()
-        device_ids = host.to(self.device, non_blocking=True)
-        tokens = self.run(device_ids, steps, graph=graph)
-        out = torch.empty(tokens.shape, dtype=torch.int32, pin_memory=True)
-        out.copy_(tokens, non_blocking=True)
+        """The end-to-end call: host prompts in, host tokens out ([batch, steps + 1]). The prompts go through a pinned
+        staging buffer straight into the engine's prompt buffer and the tokens come back through another; both
+        buffers are kept between calls (each call ends synchronised, so the next may refill them)."""
+        ids = np.asarray(token_ids)
+        if ids.shape != (self.batch, self.prompt):
+            raise ValueError(f"expected prompts of shape {(self.batch, self.prompt)}, got {tuple(ids.shape)}")
+        if self._pinned_ids is None:
+            self._pinned_ids = torch.empty((self.batch, self.prompt), dtype=torch.int32, pin_memory=True)
+        np.copyto(self._pinned_ids.numpy(), ids, casting="same_kind")
+        self.prompt_ids.view(self.batch, self.prompt).copy_(self._pinned_ids, non_blocking=True)
+        tokens = self._run_loaded(steps, graph)
+        if self._pinned_tokens is None or self._pinned_tokens.shape != tokens.shape:
+            self._pinned_tokens = torch.empty(tokens.shape, dtype=torch.int32, pin_memory=True)
+        self._pinned_tokens.copy_(tokens, non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
-        return out.numpy()
+        return self._pinned_tokens.numpy().copy()
