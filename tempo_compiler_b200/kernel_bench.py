@@ -50,7 +50,8 @@ def main() -> int:
     parser.add_argument("--m", type=int, default=65536)
     parser.add_argument("--n", type=int, default=3072)
     parser.add_argument("--k", type=int, default=768)
-    parser.add_argument("--epilogue", choices=["plain", "bias", "gelu", "residual"], default="gelu")
+    parser.add_argument("--epilogue", choices=["plain", "bias", "gelu", "residual", "ln", "ln_gelu"], default="gelu",
+                        help="ln / ln_gelu: the LayerNorm folded in on row statistics partials (gemm_ln_rowstats)")
     parser.add_argument("--seqs", type=int, default=64)
     parser.add_argument("--capacity", type=int, default=1152)
     parser.add_argument("--length", type=int, default=None, help="decode: cached keys per sequence (default capacity)")
@@ -67,7 +68,21 @@ def main() -> int:
     bf = torch.bfloat16
     result: dict = {"kernel": args.kernel}
 
-    if args.kernel == "gemm":
+    if args.kernel == "gemm" and args.epilogue.startswith("ln"):
+        from tempo_compiler_b200.engine import fold_layernorm
+        x = torch.randn((args.m, args.k), device=dev).to(bf)
+        w = (torch.randn((args.n, args.k), device=dev) * 0.05).to(bf)
+        gamma = torch.ones(args.k, device=dev, dtype=bf)
+        beta = torch.zeros(args.k, device=dev, dtype=bf)
+        folded, colsum, bias_folded = fold_layernorm(gamma, beta, w, None)
+        stats = torch.empty((args.m, args.k // 16, 2), dtype=torch.float32, device=dev)
+        ops.row_stats(x, stats)
+        out = torch.empty((args.m, args.n), device=dev, dtype=bf)
+        ms = _time(lambda: ops.gemm_ln_rowstats(x, folded, colsum, bias_folded, stats, gelu=args.epilogue == "ln_gelu",
+                                                out=out), args.repeats, args.warmup)
+        flops = 2.0 * args.m * args.n * args.k
+        result.update(m=args.m, n=args.n, k=args.k, epilogue=args.epilogue, ms=ms, tflops=flops / ms / 1e9)
+    elif args.kernel == "gemm":
         a = torch.randn((args.m, args.k), device=dev).to(bf)
         w = (torch.randn((args.n, args.k), device=dev) * 0.05).to(bf)
         bias = (torch.randn(args.n, device=dev) * 0.1).to(bf) if args.epilogue != "plain" else None
