@@ -7,7 +7,9 @@
 //               P over its S, O += P V with P read straight from TMEM (A operand in tensor memory) and V from shared
 //               memory. O stays in TMEM (64 columns) for the whole key loop.
 //   warps 2-5   softmax, one query row per thread: read S, mask (tiles reaching past the tile's first query only),
-//               exp2 on the special-function unit, P as BF16 pairs into TMEM, the row sum in FP32. The exponent base
+//               the row maximum (three-input max instructions), exp2 on the special-function unit of scores scaled
+//               and shifted two at a time (paired FP32), P as BF16 pairs into TMEM, the row sum in FP32 (paired
+//               adds, in the same order as one key at a time). The exponent base
 //               only moves when the row maximum grows by more than 2^8; only then are O and the sum rescaled (in
 //               TMEM), which keeps the math exact while skipping almost every rescale. At the end O / sum is written.
 //
@@ -278,21 +280,24 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           tmem_ld_32x32b_x32(buf + lane_addr + c32 * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c32 * 32));
         tmem_wait_ld();
         if (j >= it.first_masked) {
-          // Keys past the query, and past the sequence end, are masked.
+          // Keys past the query, and past the sequence end, are masked: key j * kKeys + c is kept while it is at
+          // most min(query, tokens - 1), one compare with a constant per key.
+          const int last = int(min(q_local, p.tokens - 1u)) - int(j * kKeys);
 #pragma unroll
-          for (uint32_t c = 0; c < kKeys; ++c) {
-            const uint32_t key = j * kKeys + c;
-            if (key > q_local || key >= p.tokens) sr[c] = __float_as_uint(-INFINITY);
-          }
+          for (uint32_t c = 0; c < kKeys; ++c)
+            if (int(c) > last) sr[c] = __float_as_uint(-INFINITY);
         }
-        // Eight independent partial maxima (short dependency chains), then combined.
+        // Eight independent partial maxima (short dependency chains) of three-input maxima, then combined: 32
+        // instructions for 64 keys.
+        static_assert(kKeys >= 24 && kKeys % 2 == 0, "the maximum tree takes 24 keys, then pairs");
         float mxs[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mxs[i] = __uint_as_float(sr[i]);
+        for (int i = 0; i < 8; ++i)
+          mxs[i] = fmax3(__uint_as_float(sr[3 * i]), __uint_as_float(sr[3 * i + 1]), __uint_as_float(sr[3 * i + 2]));
 #pragma unroll
-        for (uint32_t c = 8; c < kKeys; ++c) mxs[c % 8] = fmaxf(mxs[c % 8], __uint_as_float(sr[c]));
-        const float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
-                               fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
+        for (uint32_t c = 24; c < kKeys; c += 2)
+          mxs[(c / 2) % 8] = fmax3(mxs[(c / 2) % 8], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        const float mx = fmax3(fmax3(mxs[0], mxs[1], mxs[2]), fmax3(mxs[3], mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7]));
         bool rescale = false;
         float factor = 1.f;
         if (m_used == -INFINITY) {
@@ -304,20 +309,33 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           rescale = true;
         }
         const float base = m_used == -INFINITY ? 0.f : m_used * kLog2e;
-        float sums[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
+        // Four independent partial sums, key pair i (keys 2i, 2i+1) into sum i % 4, held as two pairs (sums 0 and
+        // 1, sums 2 and 3) so that paired FP32 instructions scale, shift and add two keys or two sums at once, each
+        // half rounded as its scalar form: the same values as one key at a time, in half the FP32 issue slots.
+        const uint64_t log2e2 = f2_splat(kLog2e), shift2 = f2_splat(-base);
+        uint64_t sums[2] = {f2_splat(0.f), f2_splat(0.f)};
 #pragma unroll
         for (int c16 = 0; c16 < int(kKeys / 32); ++c16) {
           uint32_t packed[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float e0 = fast_exp2(fmaf(__uint_as_float(sr[c16 * 32 + 2 * i]), kLog2e, -base));
-            const float e1 = fast_exp2(fmaf(__uint_as_float(sr[c16 * 32 + 2 * i + 1]), kLog2e, -base));
-            sums[i % 4] += e0 + e1;
-            packed[i] = pack_bf16x2(e0, e1);
+          for (int i = 0; i < 16; i += 2) {
+            const uint32_t c = c16 * 32 + 2 * i;
+            float a0, a1, b0, b1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), log2e2, shift2), a0, a1);
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3])), log2e2, shift2), b0,
+                      b1);
+            const float ea0 = fast_exp2(a0), ea1 = fast_exp2(a1), eb0 = fast_exp2(b0), eb1 = fast_exp2(b1);
+            packed[i] = pack_bf16x2(ea0, ea1);
+            packed[i + 1] = pack_bf16x2(eb0, eb1);
+            // (pair i's sum, pair i+1's sum) into (sum i % 4, sum (i+1) % 4)
+            sums[(i / 2) % 2] = f2_add(sums[(i / 2) % 2], f2_add(f2_pack(ea0, eb0), f2_pack(ea1, eb1)));
           }
           tmem_st_32x32b_x16(buf + lane_addr + c16 * 16, packed);
         }
-        l += (sums[0] + sums[1]) + (sums[2] + sums[3]);
+        float s0, s1, s2, s3;
+        f2_unpack(sums[0], s0, s1);
+        f2_unpack(sums[1], s2, s3);
+        l += (s0 + s1) + (s2 + s3);
         // The rescale must wait for the previous P V (the only MMA writing O) to finish.
         const bool warp_rescale = __any_sync(0xFFFFFFFFu, rescale);
         if (warp_rescale) {

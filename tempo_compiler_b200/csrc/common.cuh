@@ -119,7 +119,20 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ uint64_t f2_splat(float c) { return f2_pack(c, c); }
+
+// The largest of three floats in one instruction (PTX max.f32 with three inputs, sm_100 and later); a NaN operand is
+// ignored, as by fmaxf.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 
 // gelu_erf of two values with paired instructions: the same operations in the same order, so the same results, in
 // about half the FP32 issue slots.
