@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import argparse
 import concurrent.futures
+import fcntl
 import os
 import pathlib
 import shutil
@@ -62,13 +63,23 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> pathlib.Path:
     if not force and not verbose_ptxas and not _stale():
         return LIBRARY
     BUILD.mkdir(exist_ok=True)
+    # Several processes (one per GPU) may find the library stale at once: one builds, the others wait for it and
+    # then find it fresh. The lock also keeps them from writing the same object files.
+    with open(BUILD / ".lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        if not force and not verbose_ptxas and not _stale():
+            return LIBRARY
+        return _build_locked(verbose_ptxas)
+
+
+def _build_locked(verbose_ptxas: bool) -> pathlib.Path:
     workers = min(len(sources()), os.cpu_count() or 4)
     with concurrent.futures.ThreadPoolExecutor(max_workers=workers) as pool:
         results = list(pool.map(lambda s: _compile(s, verbose_ptxas), sources()))
     if verbose_ptxas:
         for _, log in results:
             sys.stderr.write(log)
-    tmp = LIBRARY.with_suffix(".so.tmp")
+    tmp = LIBRARY.with_suffix(f".so.{os.getpid()}.tmp")
     cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *[str(obj) for obj, _ in results]]
     result = subprocess.run(cmd, capture_output=True, text=True)
     if result.returncode != 0:
